@@ -1,0 +1,429 @@
+"""Benchmark of torch.ops.vectra.rbf_attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C]
+                    [--impl vectra|reference]
+
+One step is one pass of the operator over one batch of the workload
+(default: BASELINE config 2, the serving shape B=1024, H=8, Lq=1, Lk=64,
+D=64, bf16). With N GPUs (torchrun, one process per GPU) every rank
+processes its own batch of the same size (weak scaling; queries are
+independent, there is no collective on the data path) and the value is the
+total queries of all ranks divided by the slowest rank's device time.
+
+Rank 0 prints one JSON line with:
+* value: queries/s (or TFLOP/s for config 4), inputs resident in HBM,
+  CUDA events over exactly K steps bracketed by barrier + synchronize;
+* e2e: the same metric through the public API with pinned host buffers,
+  host->device input copies and the device->host output copy inside the
+  timed region;
+* roofline: the kernel's algorithmic bytes (or FLOPs) per launch over its
+  event-timed launch duration, against MEASURED_PEAKS.json;
+* cpu_baseline: the oracle's port of the reference operator's CPU
+  implementation (reference.matmul_rbf_attention, the default impl of
+  vectra::rbf_attention) timed on this host's cores on a bounded sample
+  (rank 0, N == 1 only);
+* clocks: nvidia-smi samples taken while the GPU ran the kernel.
+
+`--impl reference` times the reference's CPU implementation of the path
+(the operator's default impl, kernels/vectra_kernels/custom_ops.py:52-72 ->
+reference.matmul_rbf_attention, reference.py:79-99, through the oracle's
+NumPy port: the reference is Python and ships no compiled CPU code; the
+port is also ~2.6x faster here than the port of the eager chain) with all
+host threads on bounded samples of the same workload.
+"""
+
+import argparse
+import concurrent.futures
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=2000)
+    p.add_argument('--warmup', type=int, default=20)
+    p.add_argument('--config', type=int, default=2, choices=(1, 2, 3, 4))
+    p.add_argument('--impl', default='vectra', choices=('vectra',
+                                                         'reference'))
+    p.add_argument('--e2e-steps', type=int, default=20)
+    p.add_argument('--cpu-seconds', type=float, default=10.0)
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    return p.parse_args(argv)
+
+
+# ---------------------------------------------------------------------------
+# Shared descriptions
+# ---------------------------------------------------------------------------
+
+def metric_for(config):
+    if config == 4:
+        return ('RBF-attn TFLOP/s, long sequences (B=16 H=16 L=4096 D=128 '
+                'bf16)', 'TFLOP/s')
+    return ('RBF-attn queries/s @B=1024 + achieved HBM GB/s vs 8 TB/s, '
+            '1/2/4/8 B200', 'queries/s')
+
+
+def peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    try:
+        with open(path, encoding='utf-8') as f:
+            d = json.load(f)
+        return d['hbm_gbs'], d['bf16_tflops'], 'measured'
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 'fallback'
+
+
+def ncu_traffic(config):
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, 'profiles', f'ncu_config{config}.txt')
+    try:
+        with open(path, encoding='utf-8') as f:
+            for line in f:
+                m = re.match(r'dram_bytes_per_launch_full:\s*([0-9.eE+]+)',
+                             line.strip())
+                if m:
+                    return float(m.group(1))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference formulation through the oracle port.
+# ---------------------------------------------------------------------------
+
+def cpu_sample(config, n_queries, seed=1):
+    """A bounded host-side sample of the workload (same generator rules)."""
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+    w = workloads.make(config, device='cpu', seed=seed,
+                       batch=n_queries if config != 4 else 1)
+    tensors = [None if t is None else t.float().numpy() for t in w.tensors()]
+    return w, tensors
+
+
+def time_cpu(config, seconds, threads):
+    """Queries/s (or TFLOP/s) of the oracle's port of the operator's CPU
+    implementation on `threads` host threads, over a bounded sample for
+    about `seconds`."""
+    sys.path.insert(0, ROOT)
+    from oracle import rbf_oracle  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+    if config == 4:
+        # One (b, h) plane slice: 256 query rows against all 4096 keys.
+        w, (q, k, v, s, b) = cpu_sample(4, 1)
+        q, k, v = q[:, :1, :256], k[:, :1], v[:, :1]
+        s = s[:, :1]
+        flops = 2 * 256 * 4096 * (128 + 128)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds:
+            rbf_oracle.matmul_rbf_attention(q, k, v, s)
+            n += 1
+        dt = time.perf_counter() - t0
+        return (n * flops / dt / 1e12, 'TFLOP/s', 1,
+                'matmul port, 1 plane x 256 queries x 4096 keys')
+    sample = 256 if config != 1 else 8
+    w, (q, k, v, s, b) = cpu_sample(config, sample)
+    chunks = np.array_split(np.arange(q.shape[0]), threads)
+    chunks = [c for c in chunks if len(c)]
+
+    def work(idx):
+        sq, sk, sv, ss, sb = rbf_oracle.sample_planes(q, k, v, s, b, idx)
+        rbf_oracle.matmul_rbf_attention(sq, sk, sv, ss, sb)
+
+    with concurrent.futures.ThreadPoolExecutor(len(chunks)) as pool:
+        list(pool.map(work, chunks))  # warm-up
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds:
+            list(pool.map(work, chunks))
+            n += 1
+        dt = time.perf_counter() - t0
+    del workloads
+    return (n * q.shape[0] / dt, 'queries/s', len(chunks),
+            f'matmul port (the op CPU impl), {q.shape[0]} queries x {n} '
+            'repeats')
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return 0
+    metric, unit = metric_for(args.config)
+    threads = os.cpu_count() or 1
+    per_step = max(0.2, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        time_cpu(args.config, per_step / 4, threads)
+    vals = []
+    for _ in range(args.steps):
+        v, u, cores, sample = time_cpu(args.config, per_step, threads)
+        vals.append(v)
+    value = float(statistics.median(vals))
+    line = {
+        'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
+        'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'f32', 'data': 'synthetic (seeded, BASELINE config shapes)',
+        'config': {'workload': f'config{args.config}', 'device': 'host CPU'},
+        'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
+                         'kind': 'port', 'sample': sample},
+        'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
+                'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples every 100 ms."""
+
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,'
+             'clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+             'clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,'
+             'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.device = device_index
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--id={device_index}',
+                 f'--query-gpu={self.QUERY}', '--format=csv,noheader,nounits',
+                 '-lms', '100'], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [],
+                    'samples': 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(',') for r in out.strip().splitlines() if r.strip()]
+        sm, smax, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
+                 'sw_power_cap']
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+                for name, flag in zip(names, r[5:9]):
+                    if flag.strip().lower() == 'active':
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        loaded = [x for x in sm if smax and x > 0.5 * smax] or sm
+        return {'sm_mhz': statistics.median(loaded) if loaded else None,
+                'sm_max_mhz': smax, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def run_vectra(args):
+    import torch  # pylint: disable=import-outside-toplevel
+    import torch.distributed as dist  # pylint: disable=import-outside-toplevel
+    sys.path.insert(0, ROOT)
+    import vectra_b200  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    distributed = world > 1
+    if distributed:
+        import datetime  # pylint: disable=import-outside-toplevel
+        dist.init_process_group('nccl', device_id=dev,
+                                timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if distributed:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if distributed:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Weak scaling: every rank has its own batch of the configured size.
+    sets = []
+    w0 = workloads.make(args.config, device=dev, seed=1000 * rank)
+    set_bytes = workloads.dense_bytes(w0)
+    n_sets = max(1, min(8, -(-3 * L2_BYTES // set_bytes)))
+    sets.append(w0)
+    for i in range(1, n_sets):
+        sets.append(workloads.make(args.config, device=dev,
+                                   seed=1000 * rank + i))
+    alg_bytes = workloads.algorithmic_bytes(w0)
+    flops = workloads.algorithmic_flops(w0)
+    queries = w0.batch
+    op = torch.ops.vectra.rbf_attention
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        w = sets[i % n_sets]
+        return op(w.q, w.k, w.v, w.scale, w.key_bias)
+
+    # Warm-up (also loads the module and sets kernel attributes), then a
+    # short soak so the clock sampler sees the GPU under this load.
+    for i in range(max(3, args.warmup)):
+        step(i)
+    sampler = ClockSampler(local)
+    torch.cuda.synchronize()
+    t_soak = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_soak < 0.6:
+        step(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+
+    # Timed region: exactly K steps, plus per-launch events for the
+    # kernel's own duration.
+    launches0 = vectra_b200.launch_count()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    region0 = torch.cuda.Event(enable_timing=True)
+    region1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    region0.record(stream)
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step(i)
+        ends[i].record(stream)
+    region1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = vectra_b200.launch_count() - launches0
+    region_ms = region0.elapsed_time(region1)
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / max(
+        1, args.steps)
+    clocks = sampler.stop()
+    slowest_ms = max_over_ranks(region_ms)
+    ms_per_step = slowest_ms / args.steps
+
+    # End to end through the public API: pinned host inputs copied in,
+    # the operator, the result copied out, every step.
+    host = {name: (None if t is None else t.cpu().pin_memory())
+            for name, t in zip(('q', 'k', 'v', 'scale', 'key_bias'),
+                               w0.tensors())}
+    out_host = torch.empty((*w0.q.shape[:3], w0.v.shape[3]),
+                           dtype=w0.v.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values()
+              if t is not None)
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        dvc = {n: (None if t is None else t.to(dev, non_blocking=True))
+               for n, t in host.items()}
+        out = vectra_b200.rbf_attention(dvc['q'], dvc['k'], dvc['v'],
+                                        dvc['scale'], dvc['key_bias'])
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.e2e_steps, args.steps))
+    for _ in range(2):
+        e2e_step()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+
+    # Rank 0 reports.
+    metric, unit = metric_for(args.config)
+    hbm, tflops_peak, peak_kind = peaks()
+    if args.config == 4:
+        value = world * flops / (ms_per_step * 1e-3) / 1e12
+        e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
+        achieved = flops / (kernel_ms * 1e-3) / 1e12
+        roof = {'bound': 'tensor', 'achieved': achieved,
+                'peak': tflops_peak, 'unit': 'TFLOP/s',
+                'frac': achieved / tflops_peak, 'traffic': ncu_traffic(4),
+                'peak_kind': f'bf16 dense, {peak_kind} (burst)'}
+    else:
+        value = world * queries / (ms_per_step * 1e-3)
+        e2e_value = world * queries / (e2e_ms * 1e-3)
+        achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
+        roof = {'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
+                'unit': 'GB/s', 'frac': achieved / hbm,
+                'traffic': ncu_traffic(args.config),
+                'peak_kind': f'HBM copy, {peak_kind}',
+                'algorithmic_bytes_per_launch': alg_bytes,
+                'vs_8tbs': achieved / 8000.0}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, u, cores, sample = time_cpu(args.config, args.cpu_seconds,
+                                       os.cpu_count() or 1)
+        cpu = {'value': v, 'unit': u, 'cores': cores, 'kind': 'port',
+               'sample': sample}
+    if rank == 0:
+        line = {
+            'metric': metric, 'value': value, 'unit': unit,
+            'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms_per_step, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None,
+            'dtype': w0.dtype,
+            'data': 'synthetic (seeded; BASELINE config shapes and '
+                    'distributions)',
+            'config': {
+                'workload': workloads.NAMES[args.config],
+                'queries_per_gpu': queries, 'global_batch': queries * world,
+                'parallelism': f'batch-sharded x{world}, no collective',
+                'l2': f'{n_sets} rotating input sets of '
+                      f'{set_bytes / 1e6:.0f} MB (> L2 {L2_BYTES >> 20} MiB)',
+                'kernel': vectra_b200.kernel_for(*w0.tensors()),
+            },
+            'e2e': {'value': e2e_value, 'unit': unit,
+                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                    'steps': e2e_steps},
+            'gpu_launches': launches,
+            'kernel_ms_per_launch': kernel_ms,
+            'roofline': roof,
+            'cpu_baseline': cpu,
+            'clocks': clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if distributed:
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == 'reference':
+        return run_reference(args)
+    return run_vectra(args)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

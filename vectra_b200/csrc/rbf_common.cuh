@@ -1,0 +1,214 @@
+// rbf_common.cuh: problem description, element conversion and the PTX
+// helpers (mbarriers, bulk copies, exp2) shared by the RBF-attention kernels.
+//
+// All kernels compute, per (b, h, i),
+//   out = sum_j softmax_j(-g * ||q_i - k_j||^2 + bias_j) v_j,   g = scale[b,h]
+// with a float32 online softmax in the exp2 domain (logits are multiplied by
+// log2(e) once), following the reference kernel's loop
+// (kernels/vectra_kernels/spatial_rbf_attention.py:120-174) and its
+// `safe_max` rule for rows whose keys so far are all masked
+// (kernels/vectra_kernels/reference.py:146-152).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vectra_rbf.h"
+
+namespace vectra {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kNegInf = -__builtin_huge_valf();
+
+// Everything a kernel needs about one call, by value (kernel parameter).
+// Strides are in elements; a broadcast dimension has stride 0.
+struct RbfProblem {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  const void* scale;
+  const void* bias;  // nullptr: no bias
+  int32_t dtype;        // of q, k, v and out
+  int32_t scale_dtype;
+  int32_t bias_dtype;
+  int32_t pad_;
+  int64_t B, H, Nq, Nk, D, Dv;
+  int64_t sq[4], sk[4], sv[4], so[4];
+  int64_t ss[2];  // scale strides over (b, h)
+  int64_t sb[3];  // bias strides over (b, h, key)
+  unsigned int* err;  // device error word (see report_error)
+};
+
+// Device error word: kernels set bits here instead of trapping. It is one
+// `__device__` word per device owned by capi.cu, whose address reaches the
+// kernels through RbfProblem::err.
+enum : unsigned {
+  kErrWaitTimeout = 1u,  // an mbarrier wait ran past its iteration limit
+  kErrTmemAlloc = 2u,    // TMEM allocation did not succeed
+};
+
+__device__ __forceinline__ void report_error(unsigned int* err,
+                                             unsigned bits) {
+  if (err) atomicOr(err, bits);
+}
+
+// ---------------------------------------------------------------------------
+// Element conversion.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) {
+  return x;
+}
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) {
+  return __float2half_rn(x);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// Loads element `idx` of a scale/bias array of runtime dtype as float.
+__device__ __forceinline__ float load_any(const void* p, int dtype,
+                                          int64_t idx) {
+  switch (dtype) {
+    case VECTRA_F32:
+      return __ldg(static_cast<const float*>(p) + idx);
+    case VECTRA_F16:
+      return __half2float(__ldg(static_cast<const __half*>(p) + idx));
+    case VECTRA_BF16:
+      return __bfloat162float(
+          __ldg(static_cast<const __nv_bfloat16*>(p) + idx));
+    default:
+      return static_cast<float>(__ldg(static_cast<const double*>(p) + idx));
+  }
+}
+
+__device__ __forceinline__ float load_scale(const RbfProblem& p, int64_t b,
+                                            int64_t h) {
+  return load_any(p.scale, p.scale_dtype, b * p.ss[0] + h * p.ss[1]);
+}
+
+__device__ __forceinline__ float load_bias(const RbfProblem& p, int64_t b,
+                                           int64_t h, int64_t key) {
+  return load_any(p.bias, p.bias_dtype,
+                  b * p.sb[0] + h * p.sb[1] + key * p.sb[2]);
+}
+
+// 2^x on the SFU (ex2.approx: relative error ~2^-22; 2^-inf = +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier and bulk-copy (TMA, untiled) helpers. Waits are bounded: past
+// kWaitLimit polls they record kErrWaitTimeout and return false, so a lost
+// transfer becomes a host-visible error instead of a hung GPU.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar),
+               "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase,
+                                          unsigned int* err) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, phase)) return true;
+  report_error(err, kErrWaitTimeout);
+  return false;
+}
+
+// Global -> shared bulk copy completing `bytes` of transaction on `bar`.
+// dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src,
+                                         uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// L2 policy for data read exactly once (streamed keys and values).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
+               : "=l"(policy));
+  return policy;
+}
+
+// Kernel launchers (one per translation unit). Each returns a cudaError_t.
+cudaError_t launch_generic(const RbfProblem& p, cudaStream_t stream);
+cudaError_t launch_decode(const RbfProblem& p, cudaStream_t stream);
+// True when the decode kernel has an instantiation and the layout it needs.
+bool decode_supports(const RbfProblem& p);
+cudaError_t launch_tc(const RbfProblem& p, cudaStream_t stream);
+bool tc_supports(const RbfProblem& p);
+
+// Streaming-multiprocessor count of the current device (cached).
+int device_sm_count();
+
+}  // namespace vectra

@@ -1,0 +1,188 @@
+// rbf_generic.cu: RBF attention for any shape, stride and dtype.
+//
+// One 128-thread block per (query tile of kBQ rows, plane (b, h)), looping
+// over key tiles of kBK keys with an online softmax; Q, K, V tiles are
+// staged in shared memory as float32 (rows padded by one word so that
+// column-wise reads hit distinct banks). Distances are formed directly as
+// sum_d (q_d - k_d)^2 in float32, the eager formulation
+// (kernels/vectra_kernels/reference.py:54), which needs no clamp and keeps
+// full precision for far-apart points. Element strides are arbitrary, so
+// head-transposed views (kernels/tests/test_edges.py:103-114) need no copy.
+//
+// This kernel is the correctness backbone: every problem the specialised
+// kernels decline (odd head widths up to 512, Nq > 1 off the tensor-core
+// path, non-unit innermost strides, fp32 off the decode path) runs here.
+// Its roofline is the L2/SIMT one, not HBM; it is not a headline path.
+#include "rbf_common.cuh"
+
+namespace vectra {
+namespace {
+
+constexpr int kBQ = 16;       // query rows per block
+constexpr int kBK = 32;       // keys per tile
+constexpr int kThreads = 128; // 16 rows x 8 threads
+
+struct GenericSmem {
+  static size_t bytes(int64_t D, int64_t Dv) {
+    return sizeof(float) * (kBQ * (D + 1) + kBK * (D + 1) + kBK * Dv +
+                            kBQ * (kBK + 1) + kBQ * Dv + kBK);
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    rbf_generic_kernel(RbfProblem p, int64_t n_qtiles, int64_t n_blocks) {
+  extern __shared__ float smem[];
+  const int D = static_cast<int>(p.D);
+  const int Dv = static_cast<int>(p.Dv);
+  const int DP = D + 1;
+  float* Qs = smem;               // [kBQ][DP]
+  float* Ks = Qs + kBQ * DP;      // [kBK][DP]
+  float* Vs = Ks + kBK * DP;      // [kBK][Dv]
+  float* Ps = Vs + kBK * Dv;      // [kBQ][kBK + 1]
+  float* As = Ps + kBQ * (kBK + 1);  // [kBQ][Dv]
+  float* Bs = As + kBQ * Dv;      // [kBK]
+
+  const int tid = threadIdx.x;
+  const int r = tid >> 3;  // query row within the tile
+  const int c0 = tid & 7;  // first key column / value column of this thread
+  const T* __restrict__ q = static_cast<const T*>(p.q);
+  const T* __restrict__ k = static_cast<const T*>(p.k);
+  const T* __restrict__ v = static_cast<const T*>(p.v);
+  T* __restrict__ out = static_cast<T*>(p.out);
+
+  for (int64_t blk = blockIdx.x; blk < n_blocks; blk += gridDim.x) {
+    const int64_t plane = blk / n_qtiles;
+    const int64_t q0 = (blk % n_qtiles) * kBQ;
+    const int64_t b = plane / p.H, h = plane % p.H;
+    const T* qb = q + b * p.sq[0] + h * p.sq[1];
+    const T* kb = k + b * p.sk[0] + h * p.sk[1];
+    const T* vb = v + b * p.sv[0] + h * p.sv[1];
+
+    __syncthreads();  // the previous block's readers are done
+    for (int idx = tid; idx < kBQ * D; idx += kThreads) {
+      const int rr = idx / D, d = idx - rr * D;
+      const int64_t qi = q0 + rr;
+      Qs[rr * DP + d] =
+          qi < p.Nq ? to_f32(qb[qi * p.sq[2] + d * p.sq[3]]) : 0.f;
+    }
+    for (int idx = tid; idx < kBQ * Dv; idx += kThreads) As[idx] = 0.f;
+    // The coefficient in the exp2 domain: logit2 = -(g * log2 e) * dist.
+    const float g2 = load_scale(p, b, h) * kLog2e;
+    float m = kNegInf, l = 0.f;
+
+    for (int64_t k0 = 0; k0 < p.Nk; k0 += kBK) {
+      __syncthreads();  // previous tile fully consumed
+      for (int idx = tid; idx < kBK * D; idx += kThreads) {
+        const int cc = idx / D, d = idx - cc * D;
+        const int64_t kj = k0 + cc;
+        Ks[cc * DP + d] =
+            kj < p.Nk ? to_f32(kb[kj * p.sk[2] + d * p.sk[3]]) : 0.f;
+      }
+      for (int idx = tid; idx < kBK * Dv; idx += kThreads) {
+        const int cc = idx / Dv, d = idx - cc * Dv;
+        const int64_t kj = k0 + cc;
+        Vs[cc * Dv + d] =
+            kj < p.Nk ? to_f32(vb[kj * p.sv[2] + d * p.sv[3]]) : 0.f;
+      }
+      if (tid < kBK) {
+        const int64_t kj = k0 + tid;
+        float bias = kNegInf;  // keys past the end are masked
+        if (kj < p.Nk) bias = p.bias ? load_bias(p, b, h, kj) * kLog2e : 0.f;
+        Bs[tid] = bias;
+      }
+      __syncthreads();
+
+      // Scores for row r, keys c0 + 8 i.
+      float s[kBK / 8];
+      float tmax = kNegInf;
+#pragma unroll
+      for (int i = 0; i < kBK / 8; ++i) {
+        const int cc = c0 + 8 * i;
+        const float* qr = Qs + r * DP;
+        const float* kr = Ks + cc * DP;
+        float dist = 0.f;
+        for (int d = 0; d < D; ++d) {
+          const float diff = qr[d] - kr[d];
+          dist = fmaf(diff, diff, dist);
+        }
+        // -inf bias stays -inf; keys past Nk carry a -inf bias.
+        s[i] = fmaf(-g2, dist, Bs[cc]);
+        tmax = fmaxf(tmax, s[i]);
+      }
+      // Row max and sum over the 8 threads of row r (adjacent lanes).
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1)
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float m_new = fmaxf(m, tmax);
+      const float safe = (m_new == kNegInf) ? 0.f : m_new;
+      const float alpha = fast_exp2(m - safe);
+      float psum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kBK / 8; ++i) {
+        const float pr = fast_exp2(s[i] - safe);
+        Ps[r * (kBK + 1) + c0 + 8 * i] = pr;
+        psum += pr;
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1)
+        psum += __shfl_xor_sync(0xffffffffu, psum, o);
+      l = l * alpha + psum;
+      m = m_new;
+      __syncthreads();  // Ps complete
+
+      // As[r][d] = alpha * As[r][d] + sum_c P[r][c] V[c][d].
+      for (int d = c0; d < Dv; d += 8) {
+        float acc = As[r * Dv + d] * alpha;
+#pragma unroll 8
+        for (int cc = 0; cc < kBK; ++cc)
+          acc = fmaf(Ps[r * (kBK + 1) + cc], Vs[cc * Dv + d], acc);
+        As[r * Dv + d] = acc;
+      }
+    }
+
+    // out = acc / l. Fully masked rows: 0 / 0 = NaN, like the reference;
+    // no keys at all (Nk == 0): zeros, like softmax(empty) @ v.
+    const int64_t qi = q0 + r;
+    if (qi < p.Nq) {
+      const float inv = (p.Nk == 0) ? 0.f : 1.f / l;
+      T* orow = out + b * p.so[0] + h * p.so[1] + qi * p.so[2];
+      for (int d = c0; d < Dv; d += 8)
+        orow[d * p.so[3]] = from_f32<T>(As[r * Dv + d] * inv);
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_generic_t(const RbfProblem& p, cudaStream_t stream) {
+  const int64_t n_qtiles = (p.Nq + kBQ - 1) / kBQ;
+  const int64_t n_blocks = n_qtiles * p.B * p.H;
+  if (n_blocks == 0) return cudaSuccess;
+  const size_t smem = GenericSmem::bytes(p.D, p.Dv);
+  cudaError_t err = cudaFuncSetAttribute(
+      rbf_generic_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  // Enough resident blocks to fill the GPU; the kernel strides over the rest.
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+  const unsigned grid =
+      static_cast<unsigned>(n_blocks < cap ? n_blocks : cap);
+  rbf_generic_kernel<T><<<grid, kThreads, smem, stream>>>(p, n_qtiles,
+                                                          n_blocks);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_generic(const RbfProblem& p, cudaStream_t stream) {
+  switch (p.dtype) {
+    case VECTRA_F32:
+      return launch_generic_t<float>(p, stream);
+    case VECTRA_F16:
+      return launch_generic_t<__half>(p, stream);
+    default:
+      return launch_generic_t<__nv_bfloat16>(p, stream);
+  }
+}
+
+}  // namespace vectra

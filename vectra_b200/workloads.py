@@ -1,0 +1,158 @@
+"""Seeded synthetic inputs for the BASELINE configurations, and their
+algorithmic byte / FLOP counts (the roofline numerators).
+
+The reference measures on generated data too (kernels/benchmarks/
+throughput.py:97-111 `problem`); these generators follow BASELINE.json's
+config descriptions instead, with fixed seeds:
+
+1. CPU-scale serving: B=8, H=4, Lq=1, Lk=16, D=32, fp32; q,k,v ~ N(0,1);
+   gamma_h ~ U(0.05, 0.5); no mask.
+2. Serving: B=1024, H=8, Lq=1, Lk=64, D=64, bf16; q,k,v ~ N(0,1)/sqrt(D);
+   gamma_h ~ U(0.1, 1.0); dense.
+3. Variable comparable counts: B=4096, H=8, Lq=1, Lk_max=128, D=64, bf16;
+   valid length ~ U{8..128} as a 0/-inf bf16 key_bias [B,1,1,128] built
+   like the model's (models/price_transformer/model.py:233-236); keys are
+   cluster centres N(0,1) (8 per plane) plus N(0, 0.1) jitter; q ~ N(0,1);
+   v ~ N(0,1)/sqrt(D); gamma_h ~ U(0.1, 2.0).
+4. Long sequences: B=16, H=16, Lq=Lk=4096, D=128, bf16;
+   q,k,v ~ N(0,1)/sqrt(D); gamma_h ~ U(0.01, 0.2); no mask.
+"""
+
+import dataclasses
+import math
+
+import torch
+
+DTYPES = {'f32': torch.float32, 'f16': torch.float16, 'bf16': torch.bfloat16}
+
+SHAPES = {  # B, H, Nq, Nk, D, dtype
+    1: (8, 4, 1, 16, 32, 'f32'),
+    2: (1024, 8, 1, 64, 64, 'bf16'),
+    3: (4096, 8, 1, 128, 64, 'bf16'),
+    4: (16, 16, 4096, 4096, 128, 'bf16'),
+}
+NAMES = {
+    1: 'config1 B=8 H=4 Lq=1 Lk=16 D=32 fp32',
+    2: 'serving B=1024 H=8 Lq=1 Lk=64 D=64 bf16',
+    3: 'variable-count B=4096 H=8 Lq=1 Lk_max=128 D=64 bf16 padding bias',
+    4: 'long B=16 H=16 Lq=Lk=4096 D=128 bf16',
+}
+
+
+@dataclasses.dataclass
+class Workload:
+    config: int
+    dtype: str
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    scale: torch.Tensor
+    key_bias: torch.Tensor | None
+    lengths: torch.Tensor | None  # valid keys per batch row (config 3)
+
+    @property
+    def batch(self) -> int:
+        return self.q.shape[0]
+
+    def tensors(self):
+        return self.q, self.k, self.v, self.scale, self.key_bias
+
+    def slice(self, lo: int, hi: int) -> 'Workload':
+        """Batch rows [lo, hi); the scale is per head and is shared."""
+        return Workload(
+            self.config, self.dtype, self.q[lo:hi], self.k[lo:hi],
+            self.v[lo:hi], self.scale,
+            None if self.key_bias is None else self.key_bias[lo:hi],
+            None if self.lengths is None else self.lengths[lo:hi])
+
+
+def make(config: int, device='cuda', seed: int = 0,
+         batch: int | None = None) -> Workload:
+    """Builds config `config` (1-4) on `device` from `seed`.
+
+    `batch` overrides the batch size (tests use it for cheap slices); the
+    values of row b do not depend on the batch size only for config 1
+    (generation is whole-tensor).
+    """
+    B, H, nq, nk, D, dtype = SHAPES[config]
+    if batch is not None:
+        B = batch
+    td = DTYPES[dtype]
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=gen, device=device)
+
+    def rand(*shape):
+        return torch.rand(*shape, generator=gen, device=device)
+
+    lengths = bias = None
+    if config == 1:
+        q, k, v = randn(B, H, nq, D), randn(B, H, nk, D), randn(B, H, nk, D)
+        scale = 0.05 + 0.45 * rand(1, H, 1, 1)
+    elif config in (2, 4):
+        inv = 1.0 / math.sqrt(D)
+        q = randn(B, H, nq, D) * inv
+        k = randn(B, H, nk, D) * inv
+        v = randn(B, H, nk, D) * inv
+        scale = (0.1 + 0.9 * rand(1, H, 1, 1) if config == 2
+                 else 0.01 + 0.19 * rand(1, H, 1, 1))
+    elif config == 3:
+        q = randn(B, H, nq, D)
+        centres = randn(B, H, 8, D)
+        assign = torch.randint(0, 8, (B, H, nk), generator=gen,
+                               device=device)
+        k = torch.gather(centres, 2, assign[..., None].expand(B, H, nk, D))
+        k = k + 0.1 * randn(B, H, nk, D)
+        v = randn(B, H, nk, D) / math.sqrt(D)
+        scale = 0.1 + 1.9 * rand(1, H, 1, 1)
+        lengths = torch.randint(8, nk + 1, (B,), generator=gen,
+                                device=device)
+        valid = torch.arange(nk, device=device)[None, :] < lengths[:, None]
+        bias = torch.zeros(B, nk, device=device).masked_fill(
+            ~valid, float('-inf')).to(td)[:, None, None, :]
+    else:
+        raise ValueError(f'unknown config {config}')
+    return Workload(config, dtype, q.to(td), k.to(td), v.to(td), scale,
+                    bias, lengths)
+
+
+def algorithmic_bytes(w: Workload) -> int:
+    """HBM bytes one pass must move: Q, the K/V rows that carry weight,
+    O, the scale and the bias (each read or written once).
+
+    Keys masked by a -inf bias contribute nothing and are not counted
+    (config 3); without a bias every key counts.
+    """
+    B, H, nq, D = w.q.shape
+    nk, dv = w.k.shape[2], w.v.shape[3]
+    es = w.q.element_size()
+    qo = B * H * nq * (D + dv) * es
+    if w.lengths is not None:
+        keys = int(w.lengths.sum().item())
+    else:
+        keys = B * nk
+    kv = keys * H * (D + dv) * es
+    extra = w.scale.numel() * w.scale.element_size()
+    if w.key_bias is not None:
+        extra += w.key_bias.numel() * w.key_bias.element_size()
+    return qo + kv + extra
+
+
+def dense_bytes(w: Workload) -> int:
+    """Bytes if every key row were read (what the reference kernel reads)."""
+    B, H, nq, D = w.q.shape
+    nk, dv = w.k.shape[2], w.v.shape[3]
+    es = w.q.element_size()
+    extra = w.scale.numel() * w.scale.element_size()
+    if w.key_bias is not None:
+        extra += w.key_bias.numel() * w.key_bias.element_size()
+    return B * H * (nq * (D + dv) + nk * (D + dv)) * es + extra
+
+
+def algorithmic_flops(w: Workload) -> int:
+    """The two contractions, 2*Nq*Nk*(D + Dv) per plane (exponentials and
+    norms excluded, the FlashAttention convention)."""
+    B, H, nq, D = w.q.shape
+    nk, dv = w.k.shape[2], w.v.shape[3]
+    return 2 * B * H * nq * nk * (D + dv)
