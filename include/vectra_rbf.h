@@ -26,6 +26,12 @@
 
 #include <stdint.h>
 
+/* Only the functions below are exported from libvectra_rbf.so; the library
+ * is built with hidden visibility for everything else. */
+#ifndef VECTRA_API
+#define VECTRA_API __attribute__((visibility("default")))
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -102,31 +108,31 @@ typedef struct {
  * Replaces rbf_attention_forward (kernels/vectra_kernels/
  * spatial_rbf_attention.py:177-281) and the CUDA registration
  * _rbf_attention_cuda (kernels/vectra_kernels/custom_ops.py:75-85). */
-int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* stream);
+VECTRA_API int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* stream);
 
 /* Validates `args` and returns the VECTRA_KERNEL_* that forward would
  * launch, or a negative status (the same checks forward makes). Replaces
  * the tile heuristic tile_configs.select (kernels/vectra_kernels/
  * tile_configs.py:114-133). */
-int vectra_rbf_select_kernel(const vectra_rbf_args* args);
+VECTRA_API int vectra_rbf_select_kernel(const vectra_rbf_args* args);
 
 /* Name of a VECTRA_KERNEL_* value ("generic", "decode", "tc", "none"). */
-const char* vectra_rbf_kernel_name(int kernel);
+VECTRA_API const char* vectra_rbf_kernel_name(int kernel);
 
 /* Message for a status code. */
-const char* vectra_rbf_strerror(int status);
+VECTRA_API const char* vectra_rbf_strerror(int status);
 
 /* Synchronises `stream`, then reads and clears the current device's error
  * word, which kernels set instead of trapping when a bounded wait runs out.
  * Returns VECTRA_OK, VECTRA_ERR_DEVICE or VECTRA_ERR_CUDA. */
-int vectra_rbf_check_device_errors(void* stream);
+VECTRA_API int vectra_rbf_check_device_errors(void* stream);
 
 /* Kernels launched by this library in this process (all devices). Tests
  * and the benchmark use it to prove the CUDA path ran. */
-uint64_t vectra_rbf_launch_count(void);
+VECTRA_API uint64_t vectra_rbf_launch_count(void);
 
 /* Build description: version, target architecture, compiler. */
-const char* vectra_rbf_build_info(void);
+VECTRA_API const char* vectra_rbf_build_info(void);
 
 #ifdef __cplusplus
 }  /* extern "C" */

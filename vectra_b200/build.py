@@ -83,31 +83,35 @@ def _run(cmd, verbose):
 def nvcc_flags():
     return ARCH + [
         '-O3', '-lineinfo', '-std=c++17', '--expt-relaxed-constexpr',
-        '-Xcompiler', '-fPIC', '-I', INCLUDE,
+        '-Xcompiler', '-fPIC', '-Xcompiler', '-fvisibility=hidden',
+        '-I', INCLUDE,
         f'-DVECTRA_NVCC_VERSION="{_nvcc_version()}"',
     ]
 
 
-def build_library(force=False, verbose=False, extra_flags=()):
-    """Compiles the kernels and links libvectra_rbf.so."""
-    os.makedirs(BUILD, exist_ok=True)
+def build_library(force=False, verbose=False, extra_flags=(), lib_path=LIB,
+                  build_dir=BUILD):
+    """Compiles the kernels and links libvectra_rbf.so (or `lib_path`,
+    e.g. a variant built with extra -D flags into its own `build_dir`)."""
+    os.makedirs(build_dir, exist_ok=True)
     headers = _headers()
     flags = nvcc_flags() + list(extra_flags)
     objects, jobs = [], []
     for src in CU_SOURCES:
         path = os.path.join(CSRC, src)
-        obj = os.path.join(BUILD, src.replace('.cu', '.o'))
+        obj = os.path.join(build_dir, src.replace('.cu', '.o'))
         objects.append(obj)
         if force or _stale(obj, [path] + headers):
             jobs.append([_nvcc()] + flags + ['-c', path, '-o', obj])
     if jobs:
         with concurrent.futures.ThreadPoolExecutor(len(jobs)) as pool:
             list(pool.map(lambda c: _run(c, verbose), jobs))
-    if force or jobs or _stale(LIB, objects):
-        _run([_nvcc()] + ARCH + ['-shared', '-cudart', 'shared', '-o', LIB]
+    if force or jobs or _stale(lib_path, objects):
+        _run([_nvcc()] + ARCH + ['-shared', '-cudart', 'shared', '-o',
+                                 lib_path]
              + objects + ['-Xlinker', '-rpath,' +
                           os.path.join(cuda_home(), 'lib64')], verbose)
-    return LIB
+    return lib_path
 
 
 def build_torch_extension(force=False, verbose=False):

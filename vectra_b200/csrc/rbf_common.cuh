@@ -180,6 +180,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase,
   return false;
 }
 
+// Release store / acquire load of a shared-memory word (CTA scope), for
+// publishing "stage s now holds item i" between warps.
+__device__ __forceinline__ void st_release_smem(int* ptr, int v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(ptr)),
+               "r"(v)
+               : "memory");
+}
+__device__ __forceinline__ int ld_acquire_smem(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];"
+               : "=r"(v)
+               : "r"(smem_addr(ptr))
+               : "memory");
+  return v;
+}
+
+// Waits (bounded) until *ptr == want; false (error recorded) on timeout.
+__device__ __forceinline__ bool wait_smem_equals(const int* ptr, int want,
+                                                 unsigned int* err) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (ld_acquire_smem(ptr) == want) return true;
+    __nanosleep(32);
+  }
+  report_error(err, kErrWaitTimeout);
+  return false;
+}
+
 // Global -> shared bulk copy completing `bytes` of transaction on `bar`.
 // dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src,
@@ -196,6 +223,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src,
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
+               : "=l"(policy));
+  return policy;
+}
+
+// L2 policy with the default (normal) eviction priority.
+__device__ __forceinline__ uint64_t l2_evict_normal_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;"
                : "=l"(policy));
   return policy;
 }

@@ -3,181 +3,217 @@
 // comparables). HBM-bound: every byte of K and V is read exactly once.
 //
 // Design (B200):
-//  * Persistent grid, one block per SM, W warps per block. Each warp owns a
-//    ring of `ns` shared-memory stages and streams work items (plane, key
-//    chunk of KC keys) through it with untiled bulk copies
-//    (cp.async.bulk, TMA engine) completing on per-stage mbarriers, so many
-//    kilobytes per SM stay in flight without registers holding them.
-//  * Key chunks whose bias is -inf are not fetched: the warp reads the bias
-//    first and copies only rows [lo, hi] of the chunk that hold a finite
-//    bias (the variable-comparable-count config reads ~half the bytes).
-//  * Lane j owns keys j, j+32, ...: it forms sum_d (q_d - k_d)^2 from its
-//    own key row. Lanes walk the row's 16-byte chunks in a lane-rotated
-//    order, so the eight lanes of each shared-memory phase hit eight
-//    distinct bank groups (rows are contiguous, so no swizzle is possible).
+//  * Persistent grid, one block per SM. The block's shared memory is one
+//    ring of `ns` stages; work items (plane, chunk of KC keys) go to stages
+//    round-robin, item i -> stage i % ns. Each stage is filled by untiled
+//    bulk copies (cp.async.bulk, the TMA engine) that complete on the
+//    stage's mbarrier. Warps own planes (warp w of a block computes the
+//    block's planes w, w + W, ...), not stages: the warp that finishes item
+//    i refills its stage with item i + ns at once. So W warps compute while
+//    the other ns - W stages stay in flight (about 64 KB per SM sustains
+//    full HBM bandwidth), and the warp count is not tied to stage count.
+//    Because consecutive users of a stage are different warps, a parity
+//    wait alone could pass on the stage's previous phase; so the issuer
+//    publishes "stage s holds item i" (release store, after arming the
+//    mbarrier) and the consumer first waits for that word to name its
+//    item (acquire), then on the mbarrier parity.
+//  * Key chunks whose bias is -inf are not fetched: the issuing warp reads
+//    the bias first and copies only rows [lo, hi] of the chunk that hold a
+//    finite bias (the variable-comparable-count config reads ~half the
+//    bytes).
+//  * Distances: lane j owns keys j, j+32, ... and forms sum_d (q_d - k_d)^2
+//    from its own key row, with packed f32x2 subtract/FMA (two elements per
+//    instruction) into four independent accumulators. Lanes walk the row's
+//    16-byte chunks in a lane-rotated order, so the eight lanes of a
+//    shared-memory phase hit eight distinct bank groups (rows arrive
+//    contiguous from the bulk copy, so no swizzle is possible).
 //  * Softmax over a chunk is exact (max, exp2, sum with warp shuffles);
-//    chunks combine online with the reference's safe-max rule. P.V: lane
-//    owns DV/32 output columns and walks the chunk's value rows.
-//  * Norms are never materialised; the q row is converted to float32 once
-//    per plane into a bank-friendly split layout.
+//    chunks combine online with the reference's safe-max rule
+//    (kernels/vectra_kernels/reference.py:146-152).
+//  * P.V: each lane reads one 16-byte chunk of a value row per step (a warp
+//    covers 32*16 bytes = several rows per instruction) and accumulates in
+//    float32 (packed f32x2 FMA); the row groups are summed with shuffles
+//    once per plane, and the first row group stores 16 bytes per lane.
+//  * Norms are never materialised; index arithmetic is 32-bit.
 #include "rbf_common.cuh"
+
+// Stage geometry. A stage holds one work item: the q row plus KC key and
+// value rows, about VECTRA_DECODE_STAGE_BYTES. A block runs
+// VECTRA_DECODE_WARPS warps over as many stages as fit in 227 KB of shared
+// memory (at most VECTRA_DECODE_MAX_STAGES).
+#ifndef VECTRA_DECODE_STAGE_BYTES
+#define VECTRA_DECODE_STAGE_BYTES 8192
+#endif
+#ifndef VECTRA_DECODE_WARPS
+#define VECTRA_DECODE_WARPS 16
+#endif
+#ifndef VECTRA_DECODE_MAX_STAGES
+#define VECTRA_DECODE_MAX_STAGES 64
+#endif
+// 1: keys and values are copied with an L2 evict-first policy (they are
+// read exactly once); 0: default L2 policy.
+#ifndef VECTRA_DECODE_L2_EVICT_FIRST
+#define VECTRA_DECODE_L2_EVICT_FIRST 1
+#endif
 
 namespace vectra {
 namespace {
+
+// ---------------------------------------------------------------------------
+// Packed float32 pairs (sm_100a f32x2 arithmetic).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pk(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ float2 upk(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// One 32-bit word holding two elements of T as a float pair.
+template <typename T>
+__device__ __forceinline__ uint64_t widen2(uint32_t w);
+template <>
+__device__ __forceinline__ uint64_t widen2<__nv_bfloat16>(uint32_t w) {
+  return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ uint64_t widen2<__half>(uint32_t w) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return pk(f.x, f.y);
+}
+
+// A 16-byte chunk as E/2 float pairs.
+template <typename T>
+__device__ __forceinline__ void chunk_pairs(const uint4& raw, uint64_t* out) {
+  if constexpr (sizeof(T) == 4) {
+    out[0] = pk(__uint_as_float(raw.x), __uint_as_float(raw.y));
+    out[1] = pk(__uint_as_float(raw.z), __uint_as_float(raw.w));
+  } else {
+    out[0] = widen2<T>(raw.x);
+    out[1] = widen2<T>(raw.y);
+    out[2] = widen2<T>(raw.z);
+    out[3] = widen2<T>(raw.w);
+  }
+}
 
 template <typename T, int D_, int DV_, int KC_>
 struct DecodeCfg {
   static constexpr int D = D_, DV = DV_, KC = KC_;
   static constexpr int ES = sizeof(T);
-  static constexpr int E = 16 / ES;            // elements per 16-byte chunk
-  static constexpr int C = D * ES / 16;        // chunks per key row
-  static constexpr int QB = D * ES;            // bytes of the q row
-  static constexpr int KB = KC * D * ES;       // bytes of a key chunk
-  static constexpr int VB = KC * DV * ES;      // bytes of a value chunk
+  static constexpr int E = 16 / ES;           // elements per 16-byte chunk
+  static constexpr int P = E / 2;             // float pairs per chunk
+  static constexpr int C = D * ES / 16;       // chunks per key row
+  static constexpr int CV = DV * ES / 16;     // chunks per value row
+  static constexpr int RV = 32 / CV;          // value rows per warp step
+  static constexpr int QB = D * ES;           // bytes of the q row
+  static constexpr int KB = KC * D * ES;      // bytes of a key chunk
+  static constexpr int VB = KC * DV * ES;     // bytes of a value chunk
   static constexpr int STAGE = QB + KB + VB;
-  static constexpr int VE = DV / 32;           // output columns per lane
-  static constexpr int KPL = KC / 32;          // keys per lane
+  static constexpr int KPL = KC / 32;         // keys per lane
   static constexpr int ROT_DIV = C >= 8 ? 1 : 8 / C;
-  static_assert(D * ES % 16 == 0, "key rows must be whole 16-byte chunks");
-  static_assert(DV % 32 == 0 && KC % 32 == 0, "lane mapping");
-  static_assert((C & (C - 1)) == 0, "chunk count must be a power of two");
+  static_assert(D * ES % 16 == 0 && DV * ES % 16 == 0, "16-byte rows");
+  static_assert(KC % 32 == 0, "lane mapping");
+  static_assert((C & (C - 1)) == 0 && C <= 32, "key chunks: power of two");
+  static_assert((CV & (CV - 1)) == 0 && CV <= 32, "value chunks");
 
-  // Per-warp shared memory: stages, per-stage bias (exp2 domain) and key
-  // range, the float32 q row, the chunk's probabilities, the mbarriers;
-  // rounded up to 128 bytes so every warp's stages start 128-byte aligned.
-  __host__ __device__ static size_t warp_bytes(int ns) {
-    const size_t raw = size_t(ns) * STAGE + size_t(ns) * KC * 4 +
-                       size_t(ns) * 16 + D * 4 + KC * 4 + size_t(ns) * 8;
-    return (raw + 127) & ~size_t(127);
+  // Shared memory: per stage the data (128-byte aligned stride), the
+  // bias of its keys (exp2 domain), its key range and its mbarrier; per
+  // warp the float32 q row (split layout) and the chunk's probabilities.
+  static constexpr int STAGE_STRIDE = (STAGE + 127) & ~127;
+  static constexpr int STAGE_META = 8 + 16 + KC * 4;  // barrier, range, bias
+  static constexpr int WARP_BYTES = (D + KC) * 4;
+  __host__ __device__ static size_t warp_area_offset(int ns) {
+    return (size_t(ns) * (STAGE_STRIDE + STAGE_META) + 15) & ~size_t(15);
+  }
+  __host__ __device__ static size_t block_bytes(int ns, int warps) {
+    return warp_area_offset(ns) + size_t(warps) * WARP_BYTES;
   }
 };
 
-// E elements of a 16-byte chunk as float.
-template <typename T>
-__device__ __forceinline__ void unpack16(const uint4& raw, float* f);
-template <>
-__device__ __forceinline__ void unpack16<float>(const uint4& raw, float* f) {
-  f[0] = __uint_as_float(raw.x);
-  f[1] = __uint_as_float(raw.y);
-  f[2] = __uint_as_float(raw.z);
-  f[3] = __uint_as_float(raw.w);
-}
-template <>
-__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& raw,
-                                                        float* f) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-template <>
-__device__ __forceinline__ void unpack16<__half>(const uint4& raw, float* f) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
-    float2 f2 = __half22float2(h2);
-    f[2 * i] = f2.x;
-    f[2 * i + 1] = f2.y;
-  }
-}
-
-// VE consecutive elements starting at `ptr` (VE * sizeof(T) bytes aligned).
-template <typename T, int VE>
-__device__ __forceinline__ void load_slice(const uint8_t* ptr, float* f) {
-  const T* t = reinterpret_cast<const T*>(ptr);
-  if constexpr (VE * sizeof(T) == 16) {
-    unpack16<T>(*reinterpret_cast<const uint4*>(ptr), f);
-  } else if constexpr (VE * sizeof(T) == 8) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(ptr);
-    const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int i = 0; i < VE; ++i) f[i] = to_f32(e[i]);
-  } else if constexpr (VE * sizeof(T) == 4) {
-    const uint32_t raw = *reinterpret_cast<const uint32_t*>(ptr);
-    const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int i = 0; i < VE; ++i) f[i] = to_f32(e[i]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < VE; ++i) f[i] = to_f32(t[i]);
-  }
-}
-
-template <typename T, int VE>
-__device__ __forceinline__ void store_slice(T* dst, const float* f) {
-  if constexpr (VE * sizeof(T) == 4 || VE * sizeof(T) == 8 ||
-                VE * sizeof(T) == 16) {
-    union {
-      T e[VE];
-      uint32_t w[VE * sizeof(T) / 4];
-    } u;
-#pragma unroll
-    for (int i = 0; i < VE; ++i) u.e[i] = from_f32<T>(f[i]);
-    if constexpr (VE * sizeof(T) == 4) {
-      *reinterpret_cast<uint32_t*>(dst) = u.w[0];
-    } else if constexpr (VE * sizeof(T) == 8) {
-      *reinterpret_cast<uint2*>(dst) = make_uint2(u.w[0], u.w[1]);
-    } else {
-      *reinterpret_cast<uint4*>(dst) =
-          make_uint4(u.w[0], u.w[1], u.w[2], u.w[3]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < VE; ++i) dst[i] = from_f32<T>(f[i]);
-  }
-}
+struct DecodeLaunch {
+  int ns;          // stages in the block's ring
+  int n_planes;    // B * H
+  int H;
+  int nchunks;     // ceil(Nk / KC)
+  int k_contig;    // key rows adjacent in memory (one copy per chunk)
+  int v_contig;
+};
 
 template <typename T, int D, int DV, int KC>
-__global__ void __launch_bounds__(256, 1)
-    rbf_decode_kernel(RbfProblem p, int ns, int64_t n_planes, int k_rows_contig,
-                      int v_rows_contig) {
+__global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
+    rbf_decode_kernel(RbfProblem p, DecodeLaunch L) {
   using Cfg = DecodeCfg<T, D, DV, KC>;
-  constexpr int ES = Cfg::ES, E = Cfg::E, C = Cfg::C, QB = Cfg::QB;
-  constexpr int KPL = Cfg::KPL, VE = Cfg::VE;
+  constexpr int ES = Cfg::ES, E = Cfg::E, P = Cfg::P, C = Cfg::C;
+  constexpr int CV = Cfg::CV, RV = Cfg::RV, QB = Cfg::QB, KPL = Cfg::KPL;
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int W = blockDim.x >> 5;
-  const int64_t gw = int64_t(blockIdx.x) * W + warp;
-  const int64_t nw = int64_t(gridDim.x) * W;
-  if (gw >= n_planes) return;  // warps are independent: no block barrier
-
-  uint8_t* base = smem + size_t(warp) * Cfg::warp_bytes(ns);
-  uint8_t* stages = base;
-  float* meta_bias = reinterpret_cast<float*>(base + size_t(ns) * Cfg::STAGE);
-  int* meta_rng = reinterpret_cast<int*>(meta_bias + ns * KC);
-  float* q32 = reinterpret_cast<float*>(meta_rng + 4 * ns);
+  const int ns = L.ns;
+  // Layout (Cfg::block_bytes): stages | mbarriers | key ranges | biases |
+  // per-warp q32 and probabilities (16-byte aligned for float4 reads).
+  uint8_t* stages = smem;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + size_t(ns) * Cfg::STAGE_STRIDE);
+  int* meta_rng = reinterpret_cast<int*>(bars + ns);
+  float* meta_bias = reinterpret_cast<float*>(meta_rng + 4 * ns);
+  float* q32 = reinterpret_cast<float*>(
+                   smem + Cfg::warp_area_offset(ns)) + warp * (D + KC);
   float* pvals = q32 + D;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pvals + KC);
 
   const T* __restrict__ gq = static_cast<const T*>(p.q);
   const T* __restrict__ gk = static_cast<const T*>(p.k);
   const T* __restrict__ gv = static_cast<const T*>(p.v);
   T* __restrict__ gout = static_cast<T*>(p.out);
   const bool has_bias = p.bias != nullptr;
-  const uint64_t stream_policy = l2_evict_first_policy();
+  const uint64_t stream_policy = VECTRA_DECODE_L2_EVICT_FIRST
+                                     ? l2_evict_first_policy()
+                                     : l2_evict_normal_policy();
+  const int nk = static_cast<int>(p.Nk);
+  const int nchunks = L.nchunks;
+  // This block's planes: blockIdx.x, blockIdx.x + gridDim.x, ...; its items
+  // are (plane slot g, chunk c) -> i = g * nchunks + c.
+  const int n_slots = (L.n_planes - 1 - int(blockIdx.x)) / int(gridDim.x) + 1;
+  const int n_items = n_slots * nchunks;
 
-  const int nchunks = static_cast<int>((p.Nk + KC - 1) / KC);
-  const int64_t my_planes = (n_planes - 1 - gw) / nw + 1;
-  const int64_t n_items = my_planes * nchunks;
-
-  if (lane == 0) {
-    for (int s = 0; s < ns; ++s) mbar_init(smem_addr(&bars[s]), 1);
+  // meta_rng[4 s + 0, 1]: the key range [lo, hi] of the item in stage s;
+  // meta_rng[4 s + 2]: the item the stage was last armed for (-1: none).
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(smem_addr(&bars[s]), 1);
+      meta_rng[4 * s + 2] = -1;
+    }
     fence_barrier_init();
   }
-  __syncwarp();
+  __syncthreads();
 
-  // Starts the copies of work item `it` into stage `s`.
-  auto issue = [&](int64_t it, int s) {
-    const int64_t pi = it / nchunks;
-    const int chunk = static_cast<int>(it - pi * nchunks);
-    const int64_t plane = gw + pi * nw;
-    const int64_t b = plane / p.H, h = plane - (plane / p.H) * p.H;
-    const int64_t kbase = int64_t(chunk) * KC;
-    const int cnt = static_cast<int>(p.Nk - kbase < KC ? p.Nk - kbase : KC);
+  // Copies item i into stage i % ns (the whole warp takes part).
+  auto issue = [&](int i) {
+    const int g = i / nchunks, chunk = i - g * nchunks;
+    const int s = i % ns;
+    const int plane = int(blockIdx.x) + g * int(gridDim.x);
+    const int b = plane / L.H, h = plane - b * L.H;
+    const int kbase = chunk * KC;
+    const int cnt = min(KC, nk - kbase);
     int lo = 0, hi = cnt - 1;
     if (has_bias) {
       lo = KC;
@@ -201,20 +237,24 @@ __global__ void __launch_bounds__(256, 1)
     }
     const int nrows = hi >= lo ? hi - lo + 1 : 0;
     const uint32_t bar = smem_addr(&bars[s]);
-    uint8_t* st = stages + size_t(s) * Cfg::STAGE;
+    uint8_t* st = stages + size_t(s) * Cfg::STAGE_STRIDE;
+    __syncwarp();
     if (lane == 0) {
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(bar, QB + nrows * (D + DV) * ES);
       bulk_g2s(smem_addr(st), gq + b * p.sq[0] + h * p.sq[1], QB, bar,
                stream_policy);
+      st_release_smem(&meta_rng[4 * s + 2], i);  // stage s: item i, armed
     }
     __syncwarp();
     if (nrows > 0) {
-      const T* k0 = gk + b * p.sk[0] + h * p.sk[1] + (kbase + lo) * p.sk[2];
-      const T* v0 = gv + b * p.sv[0] + h * p.sv[1] + (kbase + lo) * p.sv[2];
+      const T* k0 = gk + b * p.sk[0] + h * p.sk[1] +
+                    int64_t(kbase + lo) * p.sk[2];
+      const T* v0 = gv + b * p.sv[0] + h * p.sv[1] +
+                    int64_t(kbase + lo) * p.sv[2];
       uint8_t* kd = st + QB + size_t(lo) * D * ES;
       uint8_t* vd = st + QB + Cfg::KB + size_t(lo) * DV * ES;
-      if (k_rows_contig) {
+      if (L.k_contig) {
         if (lane == 0)
           bulk_g2s(smem_addr(kd), k0, nrows * D * ES, bar, stream_policy);
       } else {
@@ -222,7 +262,7 @@ __global__ void __launch_bounds__(256, 1)
           bulk_g2s(smem_addr(kd + size_t(r) * D * ES), k0 + r * p.sk[2],
                    D * ES, bar, stream_policy);
       }
-      if (v_rows_contig) {
+      if (L.v_contig) {
         if (lane == 0)
           bulk_g2s(smem_addr(vd), v0, nrows * DV * ES, bar, stream_policy);
       } else {
@@ -233,173 +273,224 @@ __global__ void __launch_bounds__(256, 1)
     }
   };
 
-  const int64_t prologue = n_items < ns ? n_items : ns;
-  for (int64_t it = 0; it < prologue; ++it) issue(it, static_cast<int>(it));
+  // Prologue: the first ns items, spread over the warps.
+  for (int i = warp; i < ns && i < n_items; i += W) issue(i);
 
-  float g2 = 0.f, m = kNegInf, l = 0.f;
-  float acc[VE];
-  int64_t it = 0;
-  bool failed = false;
   const int rot = lane / Cfg::ROT_DIV;
+  const int vrow = lane / CV;        // value row within a warp step
+  const int vchunk = lane - vrow * CV;
 
-  for (; it < n_items; ++it) {
-    const int s = static_cast<int>(it % ns);
-    const uint32_t bar = smem_addr(&bars[s]);
-    if (!mbar_wait(bar, static_cast<uint32_t>((it / ns) & 1), p.err)) {
-      failed = true;
-      break;
-    }
-    const int64_t pi = it / nchunks;
-    const int chunk = static_cast<int>(it - pi * nchunks);
-    const int64_t plane = gw + pi * nw;
-    const int64_t b = plane / p.H, h = plane - (plane / p.H) * p.H;
-    const uint8_t* st = stages + size_t(s) * Cfg::STAGE;
-    const int lo = meta_rng[4 * s], hi = meta_rng[4 * s + 1];
-
-    if (chunk == 0) {
-      g2 = load_scale(p, b, h) * kLog2e;
-      m = kNegInf;
-      l = 0.f;
+  for (int g = warp; g < n_slots; g += W) {
+    const int plane = int(blockIdx.x) + g * int(gridDim.x);
+    const int b = plane / L.H, h = plane - b * L.H;
+    const float g2 = load_scale(p, b, h) * kLog2e;
+    float m = kNegInf, l = 0.f;
+    uint64_t acc[P];
 #pragma unroll
-      for (int e = 0; e < VE; ++e) acc[e] = 0.f;
-      // q32 split layout: element e of chunk ch at [(e / 4) * C + ch][e % 4].
-      const T* sq = reinterpret_cast<const T*>(st);
-      for (int d = lane; d < D; d += 32) {
-        const int ch = d / E, e = d - (d / E) * E;
-        q32[((e >> 2) * C + ch) * 4 + (e & 3)] = to_f32(sq[d]);
+    for (int e = 0; e < P; ++e) acc[e] = 0;
+
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
+      const int i = g * nchunks + chunk;
+      const int s = i % ns;
+      // First: stage s has been armed for item i (not still an earlier
+      // item); then: item i's bytes have landed.
+      if (!wait_smem_equals(&meta_rng[4 * s + 2], i, p.err) ||
+          !mbar_wait(smem_addr(&bars[s]), uint32_t((i / ns) & 1), p.err))
+        return;  // error recorded; the host reports it
+      const uint8_t* st = stages + size_t(s) * Cfg::STAGE_STRIDE;
+      const int lo = meta_rng[4 * s], hi = meta_rng[4 * s + 1];
+
+      if (chunk == 0) {
+        // q32 split layout: element e of chunk ch at
+        // [(e / 4) * C + ch][e % 4], so each lane's 16-byte reads hit its
+        // own bank group.
+        const T* sq = reinterpret_cast<const T*>(st);
+        for (int d = lane; d < D; d += 32) {
+          const int ch = d / E, e = d - (d / E) * E;
+          q32[((e >> 2) * C + ch) * 4 + (e & 3)] = to_f32(sq[d]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
-    }
 
-    // Squared distances of this lane's keys.
-    float dist[KPL];
+      // Squared distances: four partial accumulators (float pairs) per key.
+      uint64_t dacc[KPL][4];
 #pragma unroll
-    for (int t = 0; t < KPL; ++t) dist[t] = 0.f;
-    const uint8_t* ks = st + QB;
+      for (int t = 0; t < KPL; ++t)
+        dacc[t][0] = dacc[t][1] = dacc[t][2] = dacc[t][3] = 0;
+      const uint8_t* ks = st + QB;
 #pragma unroll
-    for (int cc = 0; cc < C; ++cc) {
-      const int ch = (cc + rot) & (C - 1);
-      float qv[E];
+      for (int cc = 0; cc < C; ++cc) {
+        const int ch = (cc + rot) & (C - 1);
+        uint64_t qv[P];
 #pragma unroll
-      for (int pp = 0; pp < E / 4; ++pp) {
-        const float4 t4 =
-            *reinterpret_cast<const float4*>(&q32[(pp * C + ch) * 4]);
-        qv[4 * pp] = t4.x;
-        qv[4 * pp + 1] = t4.y;
-        qv[4 * pp + 2] = t4.z;
-        qv[4 * pp + 3] = t4.w;
+        for (int pp = 0; pp < E / 4; ++pp) {
+          const float4 t4 =
+              *reinterpret_cast<const float4*>(&q32[(pp * C + ch) * 4]);
+          qv[2 * pp] = pk(t4.x, t4.y);
+          qv[2 * pp + 1] = pk(t4.z, t4.w);
+        }
+#pragma unroll
+        for (int t = 0; t < KPL; ++t) {
+          const int j = lane + 32 * t;
+          const uint4 raw = *reinterpret_cast<const uint4*>(
+              ks + size_t(j) * D * ES + ch * 16);
+          uint64_t kv[P];
+          chunk_pairs<T>(raw, kv);
+#pragma unroll
+          for (int e = 0; e < P; ++e) {
+            const uint64_t diff = sub2(qv[e], kv[e]);
+            uint64_t& a = dacc[t][(e + cc * P) & 3];
+            a = fma2(diff, diff, a);
+          }
+        }
       }
+
+      // Exact softmax of the chunk, merged online into (m, l, acc).
+      float sc[KPL];
+      float cmax = kNegInf;
 #pragma unroll
       for (int t = 0; t < KPL; ++t) {
         const int j = lane + 32 * t;
-        const uint4 raw = *reinterpret_cast<const uint4*>(
-            ks + size_t(j) * D * ES + ch * 16);
-        float kf[E];
-        unpack16<T>(raw, kf);
+        const float2 a0 = upk(dacc[t][0]), a1 = upk(dacc[t][1]);
+        const float2 a2 = upk(dacc[t][2]), a3 = upk(dacc[t][3]);
+        const float dist =
+            ((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y));
+        const float bv = has_bias ? meta_bias[s * KC + j] : 0.f;
+        sc[t] = (j >= lo && j <= hi) ? fmaf(-g2, dist, bv) : kNegInf;
+        cmax = fmaxf(cmax, sc[t]);
+      }
+      cmax = warp_max(cmax);
+      const float m_new = fmaxf(m, cmax);
+      const float safe = (m_new == kNegInf) ? 0.f : m_new;
+      const float alpha = fast_exp2(m - safe);
+      float psum = 0.f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float diff = qv[e] - kf[e];
-          dist[t] = fmaf(diff, diff, dist[t]);
+      for (int t = 0; t < KPL; ++t) {
+        const float pr = fast_exp2(sc[t] - safe);
+        pvals[lane + 32 * t] = pr;
+        psum += pr;
+      }
+      psum = warp_sum(psum);
+      l = fmaf(l, alpha, psum);
+      m = m_new;
+      __syncwarp();
+
+      // acc = alpha * acc + sum_j p_j v_j over this lane's row group.
+      const uint64_t alpha2 = pk(alpha, alpha);
+#pragma unroll
+      for (int e = 0; e < P; ++e) acc[e] = mul2(acc[e], alpha2);
+      const uint8_t* vs = st + QB + Cfg::KB + vchunk * 16;
+      uint64_t acc_b[P];
+#pragma unroll
+      for (int e = 0; e < P; ++e) acc_b[e] = 0;
+      int j = lo + vrow;
+      for (; j + RV <= hi; j += 2 * RV) {
+        const float p0 = pvals[j], p1 = pvals[j + RV];
+        const uint4 r0 =
+            *reinterpret_cast<const uint4*>(vs + size_t(j) * DV * ES);
+        const uint4 r1 =
+            *reinterpret_cast<const uint4*>(vs + size_t(j + RV) * DV * ES);
+        uint64_t v0[P], v1[P];
+        chunk_pairs<T>(r0, v0);
+        chunk_pairs<T>(r1, v1);
+        const uint64_t pp0 = pk(p0, p0), pp1 = pk(p1, p1);
+#pragma unroll
+        for (int e = 0; e < P; ++e) {
+          acc[e] = fma2(pp0, v0[e], acc[e]);
+          acc_b[e] = fma2(pp1, v1[e], acc_b[e]);
         }
       }
-    }
-
-    // Exact softmax of the chunk, merged online into (m, l, acc).
-    float sc[KPL];
-    float cmax = kNegInf;
+      if (j <= hi) {
+        const float p0 = pvals[j];
+        const uint4 r0 =
+            *reinterpret_cast<const uint4*>(vs + size_t(j) * DV * ES);
+        uint64_t v0[P];
+        chunk_pairs<T>(r0, v0);
+        const uint64_t pp0 = pk(p0, p0);
 #pragma unroll
-    for (int t = 0; t < KPL; ++t) {
-      const int j = lane + 32 * t;
-      const float bv = has_bias ? meta_bias[s * KC + j] : 0.f;
-      sc[t] = (j >= lo && j <= hi) ? fmaf(-g2, dist[t], bv) : kNegInf;
-      cmax = fmaxf(cmax, sc[t]);
-    }
-    cmax = warp_max(cmax);
-    const float m_new = fmaxf(m, cmax);
-    const float safe = (m_new == kNegInf) ? 0.f : m_new;
-    const float alpha = fast_exp2(m - safe);
-    float psum = 0.f;
-#pragma unroll
-    for (int t = 0; t < KPL; ++t) {
-      const float pr = fast_exp2(sc[t] - safe);
-      pvals[lane + 32 * t] = pr;
-      psum += pr;
-    }
-    psum = warp_sum(psum);
-    l = fmaf(l, alpha, psum);
-    m = m_new;
-    __syncwarp();
-
-#pragma unroll
-    for (int e = 0; e < VE; ++e) acc[e] *= alpha;
-    const uint8_t* vs = st + QB + Cfg::KB + size_t(lane) * VE * ES;
-    int j = lo;
-    for (; j + 3 <= hi; j += 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float pj = pvals[j + u];
-        float vf[VE];
-        load_slice<T, VE>(vs + size_t(j + u) * DV * ES, vf);
-#pragma unroll
-        for (int e = 0; e < VE; ++e) acc[e] = fmaf(pj, vf[e], acc[e]);
+        for (int e = 0; e < P; ++e) acc[e] = fma2(pp0, v0[e], acc[e]);
       }
-    }
-    for (; j <= hi; ++j) {
-      const float pj = pvals[j];
-      float vf[VE];
-      load_slice<T, VE>(vs + size_t(j) * DV * ES, vf);
 #pragma unroll
-      for (int e = 0; e < VE; ++e) acc[e] = fmaf(pj, vf[e], acc[e]);
+      for (int e = 0; e < P; ++e) {
+        const float2 a = upk(acc[e]), bb = upk(acc_b[e]);
+        acc[e] = pk(a.x + bb.x, a.y + bb.y);
+      }
+      __syncwarp();  // every lane is done with stage s and pvals
+      if (i + ns < n_items) issue(i + ns);
     }
-    __syncwarp();  // every lane is done with stage s and pvals
 
-    if (chunk == nchunks - 1) {
-      // Fully masked rows: l == 0 and acc == 0, so 0 * inf = NaN as in
-      // the reference.
+    // Sum the row groups, normalise, store 16 bytes per lane of group 0.
+    // Fully masked rows: l == 0 and acc == 0, so 0 * inf = NaN as in the
+    // reference.
+    float o[E];
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+      float2 a = upk(acc[e]);
+#pragma unroll
+      for (int off = CV; off < 32; off <<= 1) {
+        a.x += __shfl_xor_sync(0xffffffffu, a.x, off);
+        a.y += __shfl_xor_sync(0xffffffffu, a.y, off);
+      }
+      o[2 * e] = a.x;
+      o[2 * e + 1] = a.y;
+    }
+    if (vrow == 0) {
       const float inv = 1.f / l;
-      float o[VE];
+      union {
+        T e[E];
+        uint4 u;
+      } pack;
 #pragma unroll
-      for (int e = 0; e < VE; ++e) o[e] = acc[e] * inv;
-      store_slice<T, VE>(gout + b * p.so[0] + h * p.so[1] + lane * VE, o);
+      for (int e = 0; e < E; ++e) pack.e[e] = from_f32<T>(o[e] * inv);
+      *reinterpret_cast<uint4*>(gout + b * p.so[0] + h * p.so[1] +
+                                vchunk * E) = pack.u;
     }
-    if (it + ns < n_items) issue(it + ns, s);
-  }
-
-  if (failed) {
-    // Drain what is still in flight (bounded) before the block exits.
-    for (int64_t r = it + 1; r < n_items && r < it + ns; ++r)
-      mbar_wait(smem_addr(&bars[r % ns]), static_cast<uint32_t>((r / ns) & 1),
-                p.err);
   }
 }
 
 template <typename T, int D, int DV>
 struct DecodeLauncher {
-  static constexpr int KC_RAW = 16384 / ((D + DV) * int(sizeof(T)));
+  static constexpr int KC_RAW =
+      VECTRA_DECODE_STAGE_BYTES / ((D + DV) * int(sizeof(T)));
   static constexpr int KC = KC_RAW >= 128 ? 128 : (KC_RAW >= 64 ? 64 : 32);
   using Cfg = DecodeCfg<T, D, DV, KC>;
 
   static cudaError_t launch(const RbfProblem& p, cudaStream_t stream) {
-    const int ns = 2;
-    const size_t per_warp = Cfg::warp_bytes(ns);
+    const int warps = VECTRA_DECODE_WARPS;
     const size_t budget = 227 * 1024;
-    int warps = static_cast<int>(budget / per_warp);
-    if (warps > 8) warps = 8;
-    if (warps < 1) return cudaErrorInvalidConfiguration;
-    const int64_t n_planes = p.B * p.H;
-    int64_t blocks = (n_planes + warps - 1) / warps;
+    int ns = static_cast<int>(
+        (budget - 16 - size_t(warps) * Cfg::WARP_BYTES) /
+        (Cfg::STAGE_STRIDE + Cfg::STAGE_META));
+    if (ns > VECTRA_DECODE_MAX_STAGES) ns = VECTRA_DECODE_MAX_STAGES;
+    if (ns < 2) return cudaErrorInvalidConfiguration;
+    // Keep at least ~6 stages in flight while the other warps compute.
+    int warps_used = warps;
+    if (ns - warps_used < 6) warps_used = ns - 6 > 4 ? ns - 6 : (ns > 4 ? 4 : ns);
+    DecodeLaunch L;
+    L.ns = ns;
+    L.n_planes = static_cast<int>(p.B * p.H);
+    L.H = static_cast<int>(p.H);
+    L.nchunks = static_cast<int>((p.Nk + KC - 1) / KC);
+    L.k_contig = p.sk[2] == D;
+    L.v_contig = p.sv[2] == DV;
+    int64_t blocks = L.n_planes;
     const int64_t cap = device_sm_count();
     if (blocks > cap) blocks = cap;
-    const size_t smem = per_warp * warps;
+    const size_t smem = Cfg::block_bytes(ns, warps_used);
     auto kern = rbf_decode_kernel<T, D, DV, KC>;
-    cudaError_t err = cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        static_cast<int>(smem));
-    if (err != cudaSuccess) return err;
-    const int k_contig = p.sk[2] == D;
-    const int v_contig = p.sv[2] == DV;
-    kern<<<static_cast<unsigned>(blocks), warps * 32, smem, stream>>>(
-        p, ns, n_planes, k_contig, v_contig);
+    // The shared-memory attribute is set once per device.
+    static int configured[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+      cudaError_t err = cudaFuncSetAttribute(
+          kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          static_cast<int>(smem));
+      if (err != cudaSuccess) return err;
+      if (dev >= 0 && dev < 64) configured[dev] = 1;
+    }
+    kern<<<static_cast<unsigned>(blocks), warps_used * 32, smem, stream>>>(p,
+                                                                           L);
     return cudaGetLastError();
   }
 };
@@ -409,12 +500,18 @@ cudaError_t dispatch_t(const RbfProblem& p, cudaStream_t stream, bool dry) {
   const int64_t d = p.D, dv = p.Dv;
   if (d != dv) return cudaErrorNotSupported;
   if constexpr (sizeof(T) == 2) {
-    if (d == 32) return dry ? cudaSuccess : DecodeLauncher<T, 32, 32>::launch(p, stream);
-    if (d == 64) return dry ? cudaSuccess : DecodeLauncher<T, 64, 64>::launch(p, stream);
-    if (d == 128) return dry ? cudaSuccess : DecodeLauncher<T, 128, 128>::launch(p, stream);
+    if (d == 32)
+      return dry ? cudaSuccess : DecodeLauncher<T, 32, 32>::launch(p, stream);
+    if (d == 64)
+      return dry ? cudaSuccess : DecodeLauncher<T, 64, 64>::launch(p, stream);
+    if (d == 128)
+      return dry ? cudaSuccess
+                 : DecodeLauncher<T, 128, 128>::launch(p, stream);
   } else {
-    if (d == 32) return dry ? cudaSuccess : DecodeLauncher<T, 32, 32>::launch(p, stream);
-    if (d == 64) return dry ? cudaSuccess : DecodeLauncher<T, 64, 64>::launch(p, stream);
+    if (d == 32)
+      return dry ? cudaSuccess : DecodeLauncher<T, 32, 32>::launch(p, stream);
+    if (d == 64)
+      return dry ? cudaSuccess : DecodeLauncher<T, 64, 64>::launch(p, stream);
   }
   return cudaErrorNotSupported;
 }
@@ -438,6 +535,9 @@ bool aligned16(const void* ptr) {
 
 bool decode_supports(const RbfProblem& p) {
   if (p.Nq != 1 || p.Nk < 1) return false;
+  // 32-bit plane and key indices.
+  if (p.B * p.H > (int64_t(1) << 30) || p.Nk > (int64_t(1) << 30))
+    return false;
   if (dispatch(p, nullptr, /*dry=*/true) != cudaSuccess) return false;
   const int64_t es = p.dtype == VECTRA_F32 ? 4 : 2;
   // Bulk copies move whole rows: unit innermost stride and 16-byte aligned
@@ -448,7 +548,7 @@ bool decode_supports(const RbfProblem& p) {
     if ((p.sq[i] * es) % 16 || (p.sk[i] * es) % 16 || (p.sv[i] * es) % 16)
       return false;
   if ((p.sk[2] * es) % 16 || (p.sv[2] * es) % 16) return false;
-  // Output: each lane stores Dv/32 consecutive elements.
+  // Output: lanes store 16-byte chunks of the row.
   if (p.so[3] != 1 || !aligned16(p.out)) return false;
   if ((p.so[0] * es) % 16 || (p.so[1] * es) % 16) return false;
   return true;
