@@ -180,6 +180,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase,
   return false;
 }
 
+// try_wait that lets the hardware suspend the thread (up to `hint_ns`)
+// until the phase completes, so waiting warps take no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar,
+                                                    uint32_t phase,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait of at most kSleepWaitLimit suspended polls of 20 us each
+// (about 2 s in all) before recording kErrWaitTimeout.
+constexpr uint32_t kSleepWaitLimit = 100000;
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t phase,
+                                                unsigned int* err) {
+  for (uint32_t i = 0; i < kSleepWaitLimit; ++i)
+    if (mbar_try_wait_sleep(bar, phase, 20000)) return true;
+  report_error(err, kErrWaitTimeout);
+  return false;
+}
+
 // Release store / acquire load of a shared-memory word (CTA scope), for
 // publishing "stage s now holds item i" between warps.
 __device__ __forceinline__ void st_release_smem(int* ptr, int v) {
@@ -196,12 +223,15 @@ __device__ __forceinline__ int ld_acquire_smem(const int* ptr) {
   return v;
 }
 
-// Waits (bounded) until *ptr == want; false (error recorded) on timeout.
+// Waits (bounded, about 2 s) until *ptr == want, backing off between
+// polls; false (error recorded) on timeout.
 __device__ __forceinline__ bool wait_smem_equals(const int* ptr, int want,
                                                  unsigned int* err) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  unsigned sleep_ns = 32;
+  for (uint32_t i = 0; i < kSleepWaitLimit; ++i) {
     if (ld_acquire_smem(ptr) == want) return true;
-    __nanosleep(32);
+    __nanosleep(sleep_ns);
+    if (sleep_ns < 512) sleep_ns <<= 1;
   }
   report_error(err, kErrWaitTimeout);
   return false;

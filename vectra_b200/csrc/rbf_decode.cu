@@ -35,21 +35,21 @@
 //    float32 (packed f32x2 FMA); the row groups are summed with shuffles
 //    once per plane, and the first row group stores 16 bytes per lane.
 //  * Norms are never materialised; index arithmetic is 32-bit.
+#include <atomic>
+
 #include "rbf_common.cuh"
 
 // Stage geometry. A stage holds one work item: the q row plus KC key and
-// value rows, about VECTRA_DECODE_STAGE_BYTES. A block runs
-// VECTRA_DECODE_WARPS warps over as many stages as fit in 227 KB of shared
-// memory (at most VECTRA_DECODE_MAX_STAGES).
-#ifndef VECTRA_DECODE_STAGE_BYTES
-#define VECTRA_DECODE_STAGE_BYTES 8192
-#endif
-#ifndef VECTRA_DECODE_WARPS
-#define VECTRA_DECODE_WARPS 16
-#endif
+// value rows. Two profiles, picked per problem: small stages (about 8 KB,
+// 16 warps) when a plane has at most two chunks of them, else large stages
+// (about 16 KB, 8 warps), so long key lists take fewer, larger items.
+// A block holds as many stages as fit in 227 KB (at most
+// VECTRA_DECODE_MAX_STAGES); warps are trimmed so about six stay in flight.
 #ifndef VECTRA_DECODE_MAX_STAGES
 #define VECTRA_DECODE_MAX_STAGES 64
 #endif
+constexpr int kSmallStageBytes = 8192, kSmallStageWarps = 16;
+constexpr int kLargeStageBytes = 16384, kLargeStageWarps = 8;
 // 1: keys and values are copied with an L2 evict-first policy (they are
 // read exactly once); 0: default L2 policy.
 #ifndef VECTRA_DECODE_L2_EVICT_FIRST
@@ -158,8 +158,8 @@ struct DecodeLaunch {
   int v_contig;
 };
 
-template <typename T, int D, int DV, int KC>
-__global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
+template <typename T, int D, int DV, int KC, int WARPS>
+__global__ void __launch_bounds__(32 * WARPS, 1)
     rbf_decode_kernel(RbfProblem p, DecodeLaunch L) {
   using Cfg = DecodeCfg<T, D, DV, KC>;
   constexpr int ES = Cfg::ES, E = Cfg::E, P = Cfg::P, C = Cfg::C;
@@ -206,7 +206,11 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
   }
   __syncthreads();
 
-  // Copies item i into stage i % ns (the whole warp takes part).
+  // Copies item i into stage i % ns (the whole warp takes part). The
+  // copies are armed by lane kIssueLane, a lane that never stores output:
+  // the release ordering of mbarrier.arrive / st.release then has no
+  // pending global store of this lane to wait for.
+  constexpr int kIssueLane = 31;
   auto issue = [&](int i) {
     const int g = i / nchunks, chunk = i - g * nchunks;
     const int s = i % ns;
@@ -231,15 +235,13 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
         }
       }
     }
-    if (lane == 0) {
-      meta_rng[4 * s] = lo;
-      meta_rng[4 * s + 1] = hi;
-    }
     const int nrows = hi >= lo ? hi - lo + 1 : 0;
     const uint32_t bar = smem_addr(&bars[s]);
     uint8_t* st = stages + size_t(s) * Cfg::STAGE_STRIDE;
     __syncwarp();
-    if (lane == 0) {
+    if (lane == kIssueLane) {
+      meta_rng[4 * s] = lo;
+      meta_rng[4 * s + 1] = hi;
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(bar, QB + nrows * (D + DV) * ES);
       bulk_g2s(smem_addr(st), gq + b * p.sq[0] + h * p.sq[1], QB, bar,
@@ -255,7 +257,7 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
       uint8_t* kd = st + QB + size_t(lo) * D * ES;
       uint8_t* vd = st + QB + Cfg::KB + size_t(lo) * DV * ES;
       if (L.k_contig) {
-        if (lane == 0)
+        if (lane == kIssueLane)
           bulk_g2s(smem_addr(kd), k0, nrows * D * ES, bar, stream_policy);
       } else {
         for (int r = lane; r < nrows; r += 32)
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
                    D * ES, bar, stream_policy);
       }
       if (L.v_contig) {
-        if (lane == 0)
+        if (lane == kIssueLane)
           bulk_g2s(smem_addr(vd), v0, nrows * DV * ES, bar, stream_policy);
       } else {
         for (int r = lane; r < nrows; r += 32)
@@ -295,7 +297,8 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
       // First: stage s has been armed for item i (not still an earlier
       // item); then: item i's bytes have landed.
       if (!wait_smem_equals(&meta_rng[4 * s + 2], i, p.err) ||
-          !mbar_wait(smem_addr(&bars[s]), uint32_t((i / ns) & 1), p.err))
+          !mbar_wait_sleep(smem_addr(&bars[s]), uint32_t((i / ns) & 1),
+                           p.err))
         return;  // error recorded; the host reports it
       const uint8_t* st = stages + size_t(s) * Cfg::STAGE_STRIDE;
       const int lo = meta_rng[4 * s], hi = meta_rng[4 * s + 1];
@@ -359,19 +362,33 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
         sc[t] = (j >= lo && j <= hi) ? fmaf(-g2, dist, bv) : kNegInf;
         cmax = fmaxf(cmax, sc[t]);
       }
-      cmax = warp_max(cmax);
+      // One butterfly reduces (max, sum of exp2 relative to that max)
+      // pairs, instead of a max reduction followed by a sum reduction.
+      float lsum = 0.f;
+      {
+        const float lsafe = (cmax == kNegInf) ? 0.f : cmax;
+#pragma unroll
+        for (int t = 0; t < KPL; ++t) lsum += fast_exp2(sc[t] - lsafe);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, cmax, off);
+        const float ol = __shfl_xor_sync(0xffffffffu, lsum, off);
+        const float nm = fmaxf(cmax, om);
+        const float ns_ = (nm == kNegInf) ? 0.f : nm;
+        lsum = lsum * fast_exp2(cmax - ns_) + ol * fast_exp2(om - ns_);
+        cmax = nm;
+      }
       const float m_new = fmaxf(m, cmax);
       const float safe = (m_new == kNegInf) ? 0.f : m_new;
       const float alpha = fast_exp2(m - safe);
-      float psum = 0.f;
+      // lsum is relative to the chunk max; rebase it to safe, like acc and
+      // l. exp2(cmax - safe) <= 1, and 0 for a fully masked chunk (where
+      // lsum is 0 too), so no inf can meet a zero here.
+      l = fmaf(l, alpha, lsum * fast_exp2(cmax - safe));
 #pragma unroll
-      for (int t = 0; t < KPL; ++t) {
-        const float pr = fast_exp2(sc[t] - safe);
-        pvals[lane + 32 * t] = pr;
-        psum += pr;
-      }
-      psum = warp_sum(psum);
-      l = fmaf(l, alpha, psum);
+      for (int t = 0; t < KPL; ++t)
+        pvals[lane + 32 * t] = fast_exp2(sc[t] - safe);
       m = m_new;
       __syncwarp();
 
@@ -384,6 +401,28 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
 #pragma unroll
       for (int e = 0; e < P; ++e) acc_b[e] = 0;
       int j = lo + vrow;
+      if (lo == 0 && hi == KC - 1) {
+        // Dense chunk: fixed trip count, fully unrolled.
+#pragma unroll
+        for (int jj = 0; jj < KC / RV; jj += 2) {
+          const int r0i = vrow + jj * RV, r1i = r0i + RV;
+          const float p0 = pvals[r0i], p1 = pvals[r1i];
+          const uint4 r0 =
+              *reinterpret_cast<const uint4*>(vs + size_t(r0i) * DV * ES);
+          const uint4 r1 =
+              *reinterpret_cast<const uint4*>(vs + size_t(r1i) * DV * ES);
+          uint64_t v0[P], v1[P];
+          chunk_pairs<T>(r0, v0);
+          chunk_pairs<T>(r1, v1);
+          const uint64_t pp0 = pk(p0, p0), pp1 = pk(p1, p1);
+#pragma unroll
+          for (int e = 0; e < P; ++e) {
+            acc[e] = fma2(pp0, v0[e], acc[e]);
+            acc_b[e] = fma2(pp1, v1[e], acc_b[e]);
+          }
+        }
+        j = hi + 1;
+      }
       for (; j + RV <= hi; j += 2 * RV) {
         const float p0 = pvals[j], p1 = pvals[j + RV];
         const uint4 r0 =
@@ -448,24 +487,28 @@ __global__ void __launch_bounds__(32 * VECTRA_DECODE_WARPS, 1)
   }
 }
 
-template <typename T, int D, int DV>
+template <int STAGE_BYTES, int D, int DV, int ES>
+constexpr int chunk_keys() {
+  return STAGE_BYTES / ((D + DV) * ES) >= 128
+             ? 128
+             : (STAGE_BYTES / ((D + DV) * ES) >= 64 ? 64 : 32);
+}
+
+template <typename T, int D, int DV, int STAGE_BYTES, int WARPS>
 struct DecodeLauncher {
-  static constexpr int KC_RAW =
-      VECTRA_DECODE_STAGE_BYTES / ((D + DV) * int(sizeof(T)));
-  static constexpr int KC = KC_RAW >= 128 ? 128 : (KC_RAW >= 64 ? 64 : 32);
+  static constexpr int KC = chunk_keys<STAGE_BYTES, D, DV, sizeof(T)>();
   using Cfg = DecodeCfg<T, D, DV, KC>;
 
   static cudaError_t launch(const RbfProblem& p, cudaStream_t stream) {
-    const int warps = VECTRA_DECODE_WARPS;
     const size_t budget = 227 * 1024;
     int ns = static_cast<int>(
-        (budget - 16 - size_t(warps) * Cfg::WARP_BYTES) /
+        (budget - 16 - size_t(WARPS) * Cfg::WARP_BYTES) /
         (Cfg::STAGE_STRIDE + Cfg::STAGE_META));
     if (ns > VECTRA_DECODE_MAX_STAGES) ns = VECTRA_DECODE_MAX_STAGES;
     if (ns < 2) return cudaErrorInvalidConfiguration;
     // Keep at least ~6 stages in flight while the other warps compute.
-    int warps_used = warps;
-    if (ns - warps_used < 6) warps_used = ns - 6 > 4 ? ns - 6 : (ns > 4 ? 4 : ns);
+    int warps = WARPS;
+    if (ns - warps < 6) warps = ns - 6 > 4 ? ns - 6 : (ns > 4 ? 4 : ns);
     DecodeLaunch L;
     L.ns = ns;
     L.n_planes = static_cast<int>(p.B * p.H);
@@ -476,42 +519,45 @@ struct DecodeLauncher {
     int64_t blocks = L.n_planes;
     const int64_t cap = device_sm_count();
     if (blocks > cap) blocks = cap;
-    const size_t smem = Cfg::block_bytes(ns, warps_used);
-    auto kern = rbf_decode_kernel<T, D, DV, KC>;
+    const size_t smem = Cfg::block_bytes(ns, warps);
+    auto kern = rbf_decode_kernel<T, D, DV, KC, WARPS>;
     // The shared-memory attribute is set once per device.
-    static int configured[64] = {0};
+    static std::atomic<int> configured[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (dev < 0 || dev >= 64 || !configured[dev].load()) {
       cudaError_t err = cudaFuncSetAttribute(
           kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
           static_cast<int>(smem));
       if (err != cudaSuccess) return err;
-      if (dev >= 0 && dev < 64) configured[dev] = 1;
+      if (dev >= 0 && dev < 64) configured[dev].store(1);
     }
-    kern<<<static_cast<unsigned>(blocks), warps_used * 32, smem, stream>>>(p,
-                                                                           L);
+    kern<<<static_cast<unsigned>(blocks), warps * 32, smem, stream>>>(p, L);
     return cudaGetLastError();
   }
 };
+
+// Small stages while a plane fits in two of them, else large stages.
+template <typename T, int D, int DV>
+cudaError_t launch_profile(const RbfProblem& p, cudaStream_t stream) {
+  using Small = DecodeLauncher<T, D, DV, kSmallStageBytes, kSmallStageWarps>;
+  using Large = DecodeLauncher<T, D, DV, kLargeStageBytes, kLargeStageWarps>;
+  if (p.Nk <= 2 * Small::KC) return Small::launch(p, stream);
+  return Large::launch(p, stream);
+}
 
 template <typename T>
 cudaError_t dispatch_t(const RbfProblem& p, cudaStream_t stream, bool dry) {
   const int64_t d = p.D, dv = p.Dv;
   if (d != dv) return cudaErrorNotSupported;
   if constexpr (sizeof(T) == 2) {
-    if (d == 32)
-      return dry ? cudaSuccess : DecodeLauncher<T, 32, 32>::launch(p, stream);
-    if (d == 64)
-      return dry ? cudaSuccess : DecodeLauncher<T, 64, 64>::launch(p, stream);
+    if (d == 32) return dry ? cudaSuccess : launch_profile<T, 32, 32>(p, stream);
+    if (d == 64) return dry ? cudaSuccess : launch_profile<T, 64, 64>(p, stream);
     if (d == 128)
-      return dry ? cudaSuccess
-                 : DecodeLauncher<T, 128, 128>::launch(p, stream);
+      return dry ? cudaSuccess : launch_profile<T, 128, 128>(p, stream);
   } else {
-    if (d == 32)
-      return dry ? cudaSuccess : DecodeLauncher<T, 32, 32>::launch(p, stream);
-    if (d == 64)
-      return dry ? cudaSuccess : DecodeLauncher<T, 64, 64>::launch(p, stream);
+    if (d == 32) return dry ? cudaSuccess : launch_profile<T, 32, 32>(p, stream);
+    if (d == 64) return dry ? cudaSuccess : launch_profile<T, 64, 64>(p, stream);
   }
   return cudaErrorNotSupported;
 }
