@@ -11,23 +11,31 @@
 // squared distance at zero (spatial_rbf_attention.py:137); that only matters
 // for near-duplicate rows and is within tolerance.
 //
-// One CTA per (b, h, tile of 128 queries); 8 warps:
-//  * warp 0, one lane: TMA producer. Q once, then K and V tiles of 128 keys
-//    into a 2-stage ring (128-byte swizzled, the canonical UMMA K-major /
-//    MN-major layouts), via 4-D tensor maps over [B, H, N, D] with the
-//    caller's strides. No multicast.
-//  * warp 1: allocates TMEM (S: 128 columns, O: Dv columns); lane 0 issues
-//    the MMAs: S = Q K^T (kind::f16, M=128, N=128, fp32 accumulate in TMEM),
-//    then O += P V once the softmax has written P (bf16, swizzled smem).
-//    tcgen05.commit signals completion on mbarriers.
-//  * warps 4-7 (one thread per query row, matching TMEM lanes 0-127):
-//    per key tile, the key norms (thread r: key r, read straight from the
-//    swizzled K tile), then tcgen05.ld of the S row, logits in the exp2
-//    domain, row max, P = exp2(logit - m) written to smem, running sum.
-//    O is rescaled in TMEM only when the row max grew by more than 8 (a
-//    factor of 256), the lazy-rescaling rule, so most tiles skip it.
-//  * Epilogue: the softmax warps read O from TMEM, divide by the running
-//    sum and store their rows.
+// One CTA per (b, h, 256 queries) = two query tiles A and B of 128 rows,
+// 12 warps in three warpgroups:
+//  * WG0 (warps 0-3) and WG1 (warps 4-7): softmax of tile A and tile B, one
+//    thread per query row (TMEM lanes 0-127). Per key tile: S is read from
+//    TMEM twice (row max, then exp2), P = exp2(logit - m) is written back
+//    into TMEM over the S columns already read (bf16 pairs), and O is
+//    rescaled in TMEM only when the row max grew by more than 8 (a factor
+//    of 256, the lazy-rescaling rule).
+//  * warp 8, one lane: TMA producer. Q (both tiles) once, then K and V tiles
+//    of 128 keys into a 2-stage ring (128-byte swizzled, the canonical UMMA
+//    K-major / MN-major layouts) via 4-D tensor maps over [B, H, N, D] with
+//    the caller's strides. No multicast.
+//  * warp 9: allocates all 512 TMEM columns (S_A, S_B, O_A, O_B); lane 0
+//    issues the MMAs, ping-ponging the tiles so the tensor core works on
+//    one tile while the other's softmax runs:
+//      QK_A(0) QK_B(0) | PV_A(t) QK_A(t+1) PV_B(t) QK_B(t+1) | ...
+//    S = Q K^T is kind::f16 with both operands in shared memory; O += P V
+//    takes P from TMEM (the TS form) and V from shared memory. MMAs of one
+//    thread execute in order, so QK_X(t+1) overwriting S_X (and P_X) runs
+//    after PV_X(t) has read P_X.
+//  * warps 10-11: key terms g log2e ||k_j||^2 - log2e b_j for each K tile
+//    (64 threads x 2 keys, read straight from the swizzled tile), published
+//    per stage through an mbarrier.
+//  * Epilogue: each softmax warpgroup reads its O from TMEM, divides by the
+//    running sum and stores its rows.
 // Every mbarrier wait is bounded (error word + early exit, no trap).
 #include <cudaTypedefs.h>
 
@@ -40,34 +48,44 @@
 namespace vectra {
 namespace {
 
-constexpr int kTileM = 128;   // query rows per CTA (TMEM lanes)
+constexpr int kTileM = 128;   // query rows per tile (TMEM lanes)
+constexpr int kTilesQ = 2;    // query tiles per CTA (A and B)
 constexpr int kTileN = 128;   // keys per tile
 constexpr int kStages = 2;    // K/V ring depth
-constexpr int kThreads = 256;
-constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 384;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kNormWarp0 = 10;
+constexpr int kNormThreads = 64;
 constexpr float kRescaleThreshold = 8.f;  // log2 of the lazy-rescale factor
 
 template <int D>
 struct TcCfg {
   static_assert(D == 64 || D == 128, "head width");
   static constexpr int KB = D / 64;                  // 128-byte column blocks
-  static constexpr int BLOCK = kTileN * 128;         // one 128-row x 128 B block
-  static constexpr int Q_BYTES = kTileM * D * 2;
+  static constexpr int BLOCK = kTileN * 128;         // 128 rows x 128 B
+  static constexpr int Q_TILE = kTileM * D * 2;
+  static constexpr int Q_BYTES = kTilesQ * Q_TILE;
   static constexpr int K_BYTES = kTileN * D * 2;
   static constexpr int V_BYTES = kTileN * D * 2;
-  static constexpr int P_BYTES = kTileM * kTileN * 2;
-  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_Q = 0;                    // + x * Q_TILE
   static constexpr int OFF_KV = OFF_Q + Q_BYTES;     // + s * STAGE
   static constexpr int STAGE = K_BYTES + V_BYTES;    // K then V
-  static constexpr int OFF_P = OFF_KV + kStages * STAGE;
-  static constexpr int OFF_NK = OFF_P + P_BYTES;     // float[2][128]
-  static constexpr int OFF_BAR = OFF_NK + 2 * kTileN * 4;
-  static constexpr int NBAR = 8 + 2 * kStages;
+  static constexpr int OFF_NK = OFF_KV + kStages * STAGE;  // float[kStages][128]
+  static constexpr int OFF_BAR = OFF_NK + kStages * kTileN * 4;
+  static constexpr int NBAR = 16;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEM + 16;
   static constexpr int SMEM_ALLOC = SMEM + 1024;     // for 1024-B alignment
-  static constexpr int TMEM_COLS = 256;              // S (128) + O (<= 128)
-  static constexpr uint32_t TMEM_O = 128;            // column of O
+  static constexpr int TMEM_COLS = 512;
+  // TMEM columns: S_A, S_B (128 each; P_X overlays the first 64 of S_X),
+  // then O_A, O_B.
+  __host__ __device__ static constexpr uint32_t s_col(int x) {
+    return uint32_t(x) * 128;
+  }
+  __host__ __device__ static constexpr uint32_t o_col(int x) {
+    return 256 + uint32_t(x) * 128;
+  }
 };
 
 // ---------------------------------------------------------------------------
@@ -114,6 +132,42 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem desc] (the TS form: A from TMEM).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem,
+                                          uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, "
+      "%7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),
+      "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]),
+      "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+// Two floats as one packed pair of T (low half = first).
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
@@ -174,22 +228,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap,
       "r"(c2), "r"(c3)
       : "memory");
 }
-// Named barrier over `count` threads that also ANDs `pred` across them, so
-// a failure seen by any thread becomes every thread's decision.
-__device__ __forceinline__ bool named_barrier_and(int id, int count,
-                                                  bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred q, p;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.and.pred p, %2, %3, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(uint32_t(pred)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format:
 // start >> 4 in bits 0-13, LBO >> 4 in 16-29, SBO >> 4 in 32-45, version 1
 // in bits 46-47, layout type 2 = SWIZZLE_128B in bits 61-63).
@@ -232,15 +270,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_addr(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-  // Barriers: 0 q_full, 1 s_full, 2 s_free, 3 p_full, 4 pv_done,
-  // 8.. kv_full[kStages], 8 + kStages.. kv_empty[kStages].
+  // Barriers: 0 q_full; 1, 2 s_full[A, B]; 3, 4 p_full[A, B];
+  // 5, 6 o_final[A, B]; 8 + s kv_full[s]; 10 + s kv_empty[s];
+  // 12 + s nk_full[s].
   const uint32_t bar_q = smem_addr(&bars[0]);
-  const uint32_t bar_s_full = smem_addr(&bars[1]);
-  const uint32_t bar_s_free = smem_addr(&bars[2]);
-  const uint32_t bar_p_full = smem_addr(&bars[3]);
-  const uint32_t bar_pv_done = smem_addr(&bars[4]);
+  auto bar_s_full = [&](int x) { return smem_addr(&bars[1 + x]); };
+  auto bar_p_full = [&](int x) { return smem_addr(&bars[3 + x]); };
+  auto bar_o_final = [&](int x) { return smem_addr(&bars[5 + x]); };
   auto bar_kv_full = [&](int s) { return smem_addr(&bars[8 + s]); };
-  auto bar_kv_empty = [&](int s) { return smem_addr(&bars[8 + kStages + s]); };
+  auto bar_kv_empty = [&](int s) { return smem_addr(&bars[10 + s]); };
+  auto bar_nk_full = [&](int s) { return smem_addr(&bars[12 + s]); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::OFF_TMEM);
   float* nk_smem = reinterpret_cast<float*>(smem + Cfg::OFF_NK);
 
@@ -249,23 +288,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int plane = blockIdx.x / P.n_qtiles;
   const int H = static_cast<int>(p.H);
   const int b = plane / H, h = plane - b * H;
-  const int q0 = qt * kTileM;
+  const int q0 = qt * (kTilesQ * kTileM);
   const int nk = static_cast<int>(p.Nk);
   const int n_tiles = P.n_ktiles;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    mbar_init(bar_s_full, 1);
-    mbar_init(bar_s_free, 4);
-    mbar_init(bar_p_full, 4);
-    mbar_init(bar_pv_done, 1);
+    for (int x = 0; x < kTilesQ; ++x) {
+      mbar_init(bar_s_full(x), 1);
+      mbar_init(bar_p_full(x), 4);
+      mbar_init(bar_o_final(x), 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar_kv_full(s), 1);
       mbar_init(bar_kv_empty(s), 1);
+      mbar_init(bar_nk_full(s), kNormThreads / 32);
     }
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
     tmem_relinquish();
   }
@@ -273,17 +314,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem;
-  const uint32_t tmem_o = tmem + Cfg::TMEM_O;
   bool ok = true;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
       mbar_arrive_expect_tx(bar_q, Cfg::Q_BYTES);
-      for (int kb = 0; kb < Cfg::KB; ++kb)
-        tma_load_4d(sbase + Cfg::OFF_Q + kb * Cfg::BLOCK, &tq, bar_q, kb * 64,
-                    q0, h, b);
+      for (int x = 0; x < kTilesQ; ++x)
+        for (int kb = 0; kb < Cfg::KB; ++kb)
+          tma_load_4d(sbase + Cfg::OFF_Q + x * Cfg::Q_TILE + kb * Cfg::BLOCK,
+                      &tq, bar_q, kb * 64, q0 + x * kTileM, h, b);
       for (int t = 0; t < n_tiles && ok; ++t) {
         const int s = t % kStages;
         ok = mbar_wait(bar_kv_empty(s), uint32_t(((t / kStages) & 1) ^ 1),
@@ -299,85 +339,98 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      ok = mbar_wait(bar_q, 0, p.err);
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        const int s = t % kStages;
-        const uint32_t st = sbase + Cfg::OFF_KV + s * Cfg::STAGE;
-        ok = mbar_wait(bar_kv_full(s), uint32_t((t / kStages) & 1), p.err);
-        if (ok && t > 0) ok = mbar_wait(bar_s_free, uint32_t((t - 1) & 1), p.err);
-        if (!ok) break;
-        tc_fence_after();
-        // S = Q K^T: K = D in steps of 16 (32 bytes inside a 128-byte row).
+      auto qk = [&](int x, int t) {
+        const uint32_t st = sbase + Cfg::OFF_KV + (t % kStages) * Cfg::STAGE;
+        const uint32_t qa = sbase + Cfg::OFF_Q + x * Cfg::Q_TILE;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * Cfg::BLOCK + (kk & 3) * 32;
-          tc_mma(tmem_s, sw128_desc(sbase + Cfg::OFF_Q + off, 16, 1024),
+          tc_mma(tmem + Cfg::s_col(x), sw128_desc(qa + off, 16, 1024),
                  sw128_desc(st + off, 16, 1024), IDESC_QK, kk > 0);
         }
-        tc_commit(bar_s_full);
-        ok = mbar_wait(bar_p_full, uint32_t(t & 1), p.err);
-        if (!ok) break;
-        tc_fence_after();
-        // O += P V: K = 128 keys in steps of 16; V is MN-major (dims
-        // contiguous): 16 keys = two 8-row groups of 128 B (SBO 1024),
+        tc_commit(bar_s_full(x));
+      };
+      auto pv = [&](int x, int t) {
+        const uint32_t vt = sbase + Cfg::OFF_KV + (t % kStages) * Cfg::STAGE +
+                            Cfg::K_BYTES;
+        // P_X: bf16 pairs in TMEM over S_X, 8 columns per 16 keys. V is
+        // MN-major: 16 keys = two 8-row groups of 128 B (SBO 1024),
         // 64-dim blocks BLOCK bytes apart (LBO).
 #pragma unroll
-        for (int kk = 0; kk < kTileN / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * Cfg::BLOCK + (kk & 3) * 32;
-          tc_mma(tmem_o, sw128_desc(sbase + Cfg::OFF_P + poff, 16, 1024),
-                 sw128_desc(st + Cfg::K_BYTES + kk * 16 * 128, Cfg::BLOCK,
-                            1024),
-                 IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(bar_pv_done);
-        tc_commit(bar_kv_empty(s));
+        for (int kk = 0; kk < kTileN / 16; ++kk)
+          tc_mma_ts(tmem + Cfg::o_col(x), tmem + Cfg::s_col(x) + kk * 8,
+                    sw128_desc(vt + kk * 16 * 128, Cfg::BLOCK, 1024),
+                    IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+      };
+      ok = mbar_wait(bar_q, 0, p.err);
+      if (ok) ok = mbar_wait(bar_kv_full(0), 0, p.err);
+      if (ok) {
+        tc_fence_after();
+        qk(0, 0);
+        qk(1, 0);
+      }
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        const int s = t % kStages;
+        const bool more = t + 1 < n_tiles;
+        const int s1 = (t + 1) % kStages;
+        ok = mbar_wait(bar_p_full(0), uint32_t(t & 1), p.err);
+        if (ok && more)
+          ok = mbar_wait(bar_kv_full(s1), uint32_t(((t + 1) / kStages) & 1),
+                         p.err);
+        if (!ok) break;
+        tc_fence_after();
+        pv(0, t);
+        if (more) qk(0, t + 1);
+        ok = mbar_wait(bar_p_full(1), uint32_t(t & 1), p.err);
+        if (!ok) break;
+        tc_fence_after();
+        pv(1, t);
+        tc_commit(bar_kv_empty(s));  // K and V of tile t are no longer read
+        if (more) qk(1, t + 1);
+      }
+      if (ok) {
+        tc_commit(bar_o_final(0));
+        tc_commit(bar_o_final(1));
       }
     }
-  } else if (warp >= kSoftmaxWarp0) {
-    // --------------------------------------------------- softmax + epilogue
-    const int r = threadIdx.x - kSoftmaxWarp0 * 32;  // query row = TMEM lane
-    const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
-    const float g = load_scale(p, b, h) * kLog2e;     // g log2(e)
-    const float a2 = 2.f * g;
-    float m_used = kNegInf, l = 0.f;
-    uint8_t* ptile = smem + Cfg::OFF_P;
-    // Every thread runs all n_tiles iterations and every named barrier; after a
-    // failed (timed-out) wait, `ok` turns false for the whole warpgroup at
-    // the next barrier and the remaining iterations skip their work. Waits
-    // are made warp-uniform so tcgen05.ld/st always run convergent.
-    for (int t = 0; t < n_tiles; ++t) {
+  } else if (warp >= kNormWarp0) {
+    // ------------------------------------------------------- key terms
+    const int th = threadIdx.x - kNormWarp0 * 32;  // 0..63
+    const float g = load_scale(p, b, h) * kLog2e;
+    for (int t = 0; t < n_tiles && ok; ++t) {
       const int s = t % kStages;
-      const uint8_t* ktile = smem + Cfg::OFF_KV + s * Cfg::STAGE;
-      float* nkb = nk_smem + (t & 1) * kTileN;
-      if (ok) ok = mbar_wait(bar_kv_full(s), uint32_t((t / kStages) & 1), p.err);
+      ok = mbar_wait(bar_kv_full(s), uint32_t((t / kStages) & 1), p.err);
       ok = __all_sync(0xffffffffu, ok);
-      // Key r's term g log2e ||k_r||^2 - log2e b_r (+inf when masked or
-      // past the end). The row's 16-byte chunks are summed in an order
-      // rotated by r % 8 so the eight rows of a phase hit distinct banks.
-      if (ok) {
+      if (!ok) break;
+      const uint8_t* ktile = smem + Cfg::OFF_KV + s * Cfg::STAGE;
+#pragma unroll
+      for (int i = 0; i < kTileN / kNormThreads; ++i) {
+        const int r = th + i * kNormThreads;
         const int key = t * kTileN + r;
-        float nv = __int_as_float(0x7f800000);
+        float nv = __int_as_float(0x7f800000);  // past the end: masked
         if (key < nk) {
           float accx = 0.f, accy = 0.f;
 #pragma unroll
           for (int kb = 0; kb < Cfg::KB; ++kb) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
+              // Chunk order rotated by r % 8: the eight rows of a phase
+              // hit distinct bank groups.
               const uint4 raw = *reinterpret_cast<const uint4*>(
                   ktile + kb * Cfg::BLOCK + r * 128 + ((c ^ (r & 7)) << 4));
               const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
+              for (int k2 = 0; k2 < 4; ++k2) {
                 float lo, hi;
                 if constexpr (FMT == 1) {
-                  lo = __uint_as_float(w[i] << 16);
-                  hi = __uint_as_float(w[i] & 0xffff0000u);
+                  lo = __uint_as_float(w[k2] << 16);
+                  hi = __uint_as_float(w[k2] & 0xffff0000u);
                 } else {
                   const float2 f = __half22float2(
-                      *reinterpret_cast<const __half2*>(&w[i]));
+                      *reinterpret_cast<const __half2*>(&w[k2]));
                   lo = f.x;
                   hi = f.y;
                 }
@@ -389,43 +442,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           nv = g * (accx + accy);
           if (p.bias) nv -= load_bias(p, b, h, key) * kLog2e;
         }
-        nkb[r] = nv;
+        nk_smem[s * kTileN + r] = nv;
       }
-      ok = named_barrier_and(1, 128, ok);
-      if (!ok) continue;
-
-      ok = mbar_wait(bar_s_full, uint32_t(t & 1), p.err);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) continue;
-      tc_fence_after();
-      float sv[kTileN];
-#pragma unroll
-      for (int c = 0; c < kTileN / 32; ++c)
-        tmem_ld32(tmem_s + lane_base + c * 32, sv + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_s_free);  // S may be overwritten
+      if (lane == 0) mbar_arrive(bar_nk_full(s));
+    }
+  } else {
+    // --------------------------------------------- softmax, tile x = A/B
+    const int x = warp >> 2;                  // 0: A (warps 0-3), 1: B
+    const int r = threadIdx.x & 127;          // query row = TMEM lane
+    const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t s_col = tmem + lane_base + Cfg::s_col(x);
+    const uint32_t o_col = tmem + lane_base + Cfg::o_col(x);
+    const float a2 = 2.f * load_scale(p, b, h) * kLog2e;
+    float m_used = kNegInf, l = 0.f;
+    for (int t = 0; t < n_tiles && ok; ++t) {
+      const int s = t % kStages;
+      const float* nkb = nk_smem + s * kTileN;
+      ok = mbar_wait(bar_s_full(x), uint32_t(t & 1), p.err) &&
+           mbar_wait(bar_nk_full(s), uint32_t((t / kStages) & 1), p.err);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // Pass 1: the row max of the logits a2 * S - nk.
       float mx = kNegInf;
 #pragma unroll
-      for (int j = 0; j < kTileN; j += 4) {
-        const float4 n4 = *reinterpret_cast<const float4*>(nkb + j);
-        sv[j] = fmaf(a2, sv[j], -n4.x);
-        sv[j + 1] = fmaf(a2, sv[j + 1], -n4.y);
-        sv[j + 2] = fmaf(a2, sv[j + 2], -n4.z);
-        sv[j + 3] = fmaf(a2, sv[j + 3], -n4.w);
-        mx = fmaxf(mx, fmaxf(fmaxf(sv[j], sv[j + 1]),
-                             fmaxf(sv[j + 2], sv[j + 3])));
-      }
-      // P(t-1) consumed and O(t-1) final before P and O are touched.
-      if (t > 0) {
-        ok = mbar_wait(bar_pv_done, uint32_t((t - 1) & 1), p.err);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) continue;
-        tc_fence_after();
+      for (int c = 0; c < kTileN / 32; ++c) {
+        float v[32];
+        tmem_ld32(s_col + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 n4 = *reinterpret_cast<const float4*>(nkb + c * 32 + j);
+          const float l0 = fmaf(a2, v[j], -n4.x);
+          const float l1 = fmaf(a2, v[j + 1], -n4.y);
+          const float l2 = fmaf(a2, v[j + 2], -n4.z);
+          const float l3 = fmaf(a2, v[j + 3], -n4.w);
+          mx = fmaxf(mx, fmaxf(fmaxf(l0, l1), fmaxf(l2, l3)));
+        }
       }
       // Lazy rescaling: move this row's reference max only when the max
-      // grew by more than 2^8; the warp rescales O if any row moved.
+      // grew by more than 2^8; the warp rescales O if any of its rows moved.
+      // (PV_X(t-1) has completed: QK_X(t) ran after it, in order.)
       const bool need = mx > m_used + kRescaleThreshold ||
                         (m_used == kNegInf && mx != kNegInf);
       float factor = 1.f;
@@ -438,53 +496,55 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           float ov[32];
-          tmem_ld32(tmem_o + lane_base + c * 32, ov);
+          tmem_ld32(o_col + c * 32, ov);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] *= factor;
-          tmem_st32(tmem_o + lane_base + c * 32, ov);
+          tmem_st32(o_col + c * 32, ov);
         }
-        tmem_wait_st();
       }
+      // Pass 2: P = exp2(logit - m), packed to pairs over the S columns
+      // already read (chunk c of S -> P columns 16c..16c+15).
       const float ref = m_used == kNegInf ? 0.f : m_used;
       float lsum = 0.f;
 #pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
+      for (int c = 0; c < kTileN / 32; ++c) {
+        float v[32];
+        tmem_ld32(s_col + c * 32, v);
+        tmem_wait_ld();
+        uint32_t pp[16];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          union {
-            T e[8];
-            uint4 u;
-          } pk8;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float pr = fast_exp2(sv[kb * 64 + c * 8 + e] - ref);
-            lsum += pr;
-            pk8.e[e] = from_f32<T>(pr);
-          }
-          *reinterpret_cast<uint4*>(ptile + kb * Cfg::BLOCK + r * 128 +
-                                    ((c ^ (r & 7)) << 4)) = pk8.u;
+        for (int j = 0; j < 32; j += 4) {
+          const float4 n4 = *reinterpret_cast<const float4*>(nkb + c * 32 + j);
+          const float e0 = fast_exp2(fmaf(a2, v[j], -n4.x) - ref);
+          const float e1 = fast_exp2(fmaf(a2, v[j + 1], -n4.y) - ref);
+          const float e2 = fast_exp2(fmaf(a2, v[j + 2], -n4.z) - ref);
+          const float e3 = fast_exp2(fmaf(a2, v[j + 3], -n4.w) - ref);
+          lsum += (e0 + e1) + (e2 + e3);
+          pp[j / 2] = pack2<T>(e0, e1);
+          pp[j / 2 + 1] = pack2<T>(e2, e3);
         }
+        tmem_st16(s_col + c * 16, pp);
       }
       l += lsum;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p_full);
+      if (lane == 0) mbar_arrive(bar_p_full(x));
     }
     // Epilogue: O / l for this row.
-    if (ok) ok = mbar_wait(bar_pv_done, uint32_t((n_tiles - 1) & 1), p.err);
+    if (ok) ok = mbar_wait(bar_o_final(x), 0, p.err);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
-      const int qrow = q0 + r;
+      const int qrow = q0 + x * kTileM + r;
       const float inv = 1.f / l;
       T* orow = static_cast<T*>(p.out) + b * p.so[0] + h * p.so[1] +
                 int64_t(qrow) * p.so[2];
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float ov[32];
-        tmem_ld32(tmem_o + lane_base + c * 32, ov);
+        tmem_ld32(o_col + c * 32, ov);
         tmem_wait_ld();
         if (qrow < p.Nq) {
 #pragma unroll
@@ -506,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Teardown: every TMEM access is done before the allocating warp frees it.
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
@@ -566,7 +626,8 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
       !make_map(&tv, p.v, p.dtype, p.B, p.H, p.Nk, D, p.sv))
     return cudaErrorInvalidValue;
   TcParams P;
-  P.n_qtiles = static_cast<int>((p.Nq + kTileM - 1) / kTileM);
+  P.n_qtiles = static_cast<int>((p.Nq + kTilesQ * kTileM - 1) /
+                               (kTilesQ * kTileM));
   P.n_ktiles = static_cast<int>((p.Nk + kTileN - 1) / kTileN);
   const int64_t blocks = int64_t(P.n_qtiles) * p.B * p.H;
   auto kern = rbf_tc_kernel<T, D>;
@@ -594,7 +655,7 @@ bool tc_supports(const RbfProblem& p) {
   if (p.dtype != VECTRA_BF16 && p.dtype != VECTRA_F16) return false;
   if (p.D != p.Dv || (p.D != 64 && p.D != 128)) return false;
   if (p.Nq < 128 || p.Nk < 128) return false;
-  if (p.B * p.H * ((p.Nq + 127) / 128) > (int64_t(1) << 31) - 1) return false;
+  if (p.B * p.H * ((p.Nq + 255) / 256) > (int64_t(1) << 31) - 1) return false;
   if (p.Nq > (int64_t(1) << 31) - 1 || p.Nk > (int64_t(1) << 31) - 1)
     return false;
   // TMA: unit innermost stride, 16-byte aligned bases and strides.
