@@ -211,6 +211,63 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
 }
+// 32 columns as raw 32-bit words (no conversion).
+__device__ __forceinline__ void tmem_ld32u(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, "
+      "%7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, "
+      "%21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+// tcgen05.wait::ld that also names the 32 destination registers of the
+// load being waited for, so no use of them is scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld_tied(uint32_t* r) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]),
+        "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]),
+        "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+        "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+        "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+__device__ __forceinline__ uint64_t f2pk(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ float2 f2upk(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -442,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           nv = g * (accx + accy);
           if (p.bias) nv -= load_bias(p, b, h, key) * kLog2e;
         }
-        nk_smem[s * kTileN + r] = nv;
+        nk_smem[s * kTileN + r] = -nv;  // stored negated: logit = a2 S + this
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_nk_full(s));
@@ -464,21 +521,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // Pass 1: the row max of the logits a2 * S - nk.
+      // Pass 1: the row max of the logits a2 * S - nk. TMEM loads are
+      // pipelined: chunk c + 1 is in flight while chunk c is processed.
+      const uint64_t a2x2 = f2pk(a2, a2);
       float mx = kNegInf;
+      {
+        uint32_t buf[2][32];
+        tmem_ld32u(s_col, buf[0]);
 #pragma unroll
-      for (int c = 0; c < kTileN / 32; ++c) {
-        float v[32];
-        tmem_ld32(s_col + c * 32, v);
-        tmem_wait_ld();
+        for (int c = 0; c < kTileN / 32; ++c) {
+          uint32_t* cur = buf[c & 1];
+          tmem_wait_ld_tied(cur);
+          if (c + 1 < kTileN / 32) tmem_ld32u(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 n4 = *reinterpret_cast<const float4*>(nkb + c * 32 + j);
-          const float l0 = fmaf(a2, v[j], -n4.x);
-          const float l1 = fmaf(a2, v[j + 1], -n4.y);
-          const float l2 = fmaf(a2, v[j + 2], -n4.z);
-          const float l3 = fmaf(a2, v[j + 3], -n4.w);
-          mx = fmaxf(mx, fmaxf(fmaxf(l0, l1), fmaxf(l2, l3)));
+          for (int j = 0; j < 32; j += 4) {
+            const float4 n4 =
+                *reinterpret_cast<const float4*>(nkb + c * 32 + j);
+            const float2 l01 = f2upk(ffma2(
+                a2x2, f2pk(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])),
+                f2pk(n4.x, n4.y)));
+            const float2 l23 = f2upk(ffma2(
+                a2x2,
+                f2pk(__uint_as_float(cur[j + 2]), __uint_as_float(cur[j + 3])),
+                f2pk(n4.z, n4.w)));
+            mx = fmax3(mx, l01.x, l01.y);
+            mx = fmax3(mx, l23.x, l23.y);
+          }
         }
       }
       // Lazy rescaling: move this row's reference max only when the max
@@ -504,28 +572,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Pass 2: P = exp2(logit - m), packed to pairs over the S columns
-      // already read (chunk c of S -> P columns 16c..16c+15).
+      // already read (chunk c of S -> P columns 16c..16c+15); TMEM loads
+      // pipelined as in pass 1.
       const float ref = m_used == kNegInf ? 0.f : m_used;
-      float lsum = 0.f;
+      const uint64_t negref2 = f2pk(-ref, -ref);
+      uint64_t lsum2a = 0, lsum2b = 0;
+      {
+        uint32_t buf[2][32];
+        tmem_ld32u(s_col, buf[0]);
 #pragma unroll
-      for (int c = 0; c < kTileN / 32; ++c) {
-        float v[32];
-        tmem_ld32(s_col + c * 32, v);
-        tmem_wait_ld();
-        uint32_t pp[16];
+        for (int c = 0; c < kTileN / 32; ++c) {
+          uint32_t* cur = buf[c & 1];
+          tmem_wait_ld_tied(cur);
+          if (c + 1 < kTileN / 32) tmem_ld32u(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
+          uint32_t pp[16];
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 n4 = *reinterpret_cast<const float4*>(nkb + c * 32 + j);
-          const float e0 = fast_exp2(fmaf(a2, v[j], -n4.x) - ref);
-          const float e1 = fast_exp2(fmaf(a2, v[j + 1], -n4.y) - ref);
-          const float e2 = fast_exp2(fmaf(a2, v[j + 2], -n4.z) - ref);
-          const float e3 = fast_exp2(fmaf(a2, v[j + 3], -n4.w) - ref);
-          lsum += (e0 + e1) + (e2 + e3);
-          pp[j / 2] = pack2<T>(e0, e1);
-          pp[j / 2 + 1] = pack2<T>(e2, e3);
+          for (int j = 0; j < 32; j += 4) {
+            const float4 n4 =
+                *reinterpret_cast<const float4*>(nkb + c * 32 + j);
+            const uint64_t b01 = fadd2(f2pk(n4.x, n4.y), negref2);
+            const uint64_t b23 = fadd2(f2pk(n4.z, n4.w), negref2);
+            const float2 x01 = f2upk(ffma2(
+                a2x2, f2pk(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])),
+                b01));
+            const float2 x23 = f2upk(ffma2(
+                a2x2,
+                f2pk(__uint_as_float(cur[j + 2]), __uint_as_float(cur[j + 3])),
+                b23));
+            const float e0 = fast_exp2(x01.x), e1 = fast_exp2(x01.y);
+            const float e2 = fast_exp2(x23.x), e3 = fast_exp2(x23.y);
+            lsum2a = fadd2(lsum2a, f2pk(e0, e1));
+            lsum2b = fadd2(lsum2b, f2pk(e2, e3));
+            pp[j / 2] = pack2<T>(e0, e1);
+            pp[j / 2 + 1] = pack2<T>(e2, e3);
+          }
+          tmem_st16(s_col + c * 16, pp);
         }
-        tmem_st16(s_col + c * 16, pp);
       }
+      const float2 la = f2upk(lsum2a), lb = f2upk(lsum2b);
+      const float lsum = (la.x + la.y) + (lb.x + lb.y);
       l += lsum;
       tmem_wait_st();
       tc_fence_before();
