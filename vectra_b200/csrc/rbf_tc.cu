@@ -58,6 +58,13 @@ constexpr int kMmaWarp = 9;
 constexpr int kNormWarp0 = 10;
 constexpr int kNormThreads = 64;
 constexpr float kRescaleThreshold = 8.f;  // log2 of the lazy-rescale factor
+// Register split (setmaxnreg): the two softmax warpgroups hold a whole S row
+// (128 values) in registers; the producer / MMA / key-term warpgroup needs
+// few. The launch gives every thread kLaunchRegs; the split must not exceed
+// that total (checked on the host against the compiled kernel before any
+// launch), or setmaxnreg.inc would wait for registers that never come.
+constexpr int kSoftmaxRegs = 200;
+constexpr int kOtherRegs = 104;
 
 template <int D>
 struct TcCfg {
@@ -242,6 +249,29 @@ __device__ __forceinline__ void tmem_wait_ld_tied(uint32_t* r) {
       :
       : "memory");
 }
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+// Orders later uses of 32 registers after a preceding tcgen05.wait::ld
+// (emits no instruction).
+__device__ __forceinline__ void regs_tie32(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]),
+                 "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]),
+                 "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 __device__ __forceinline__ uint64_t f2pk(float x, float y) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
@@ -373,6 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
+  if (warp >= kProducerWarp) {
+  setmaxnreg_dec<kOtherRegs>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
@@ -504,8 +536,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_nk_full(s));
     }
+  }
   } else {
     // --------------------------------------------- softmax, tile x = A/B
+    setmaxnreg_inc<kSoftmaxRegs>();
     const int x = warp >> 2;                  // 0: A (warps 0-3), 1: B
     const int r = threadIdx.x & 127;          // query row = TMEM lane
     const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
@@ -521,34 +555,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // Pass 1: the row max of the logits a2 * S - nk. TMEM loads are
-      // pipelined: chunk c + 1 is in flight while chunk c is processed.
+      // The whole S row into registers (four 32-column loads, one wait),
+      // turned into logits a2 * S - nk in place; the row max with four
+      // independent accumulators.
       const uint64_t a2x2 = f2pk(a2, a2);
-      float mx = kNegInf;
-      {
-        uint32_t buf[2][32];
-        tmem_ld32u(s_col, buf[0]);
+      uint32_t sv[kTileN];
 #pragma unroll
-        for (int c = 0; c < kTileN / 32; ++c) {
-          uint32_t* cur = buf[c & 1];
-          tmem_wait_ld_tied(cur);
-          if (c + 1 < kTileN / 32) tmem_ld32u(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
+      for (int c = 0; c < kTileN / 32; ++c) tmem_ld32u(s_col + c * 32, sv + c * 32);
+      tmem_wait_ld_tied(sv);
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 n4 =
-                *reinterpret_cast<const float4*>(nkb + c * 32 + j);
-            const float2 l01 = f2upk(ffma2(
-                a2x2, f2pk(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])),
-                f2pk(n4.x, n4.y)));
-            const float2 l23 = f2upk(ffma2(
-                a2x2,
-                f2pk(__uint_as_float(cur[j + 2]), __uint_as_float(cur[j + 3])),
-                f2pk(n4.z, n4.w)));
-            mx = fmax3(mx, l01.x, l01.y);
-            mx = fmax3(mx, l23.x, l23.y);
-          }
-        }
+      for (int c = 1; c < kTileN / 32; ++c) regs_tie32(sv + c * 32);
+      float mxa = kNegInf, mxb = kNegInf, mxc = kNegInf, mxd = kNegInf;
+#pragma unroll
+      for (int j = 0; j < kTileN; j += 8) {
+        const float4 n4 = *reinterpret_cast<const float4*>(nkb + j);
+        const float4 m4 = *reinterpret_cast<const float4*>(nkb + j + 4);
+        const float2 l01 = f2upk(ffma2(
+            a2x2, f2pk(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1])),
+            f2pk(n4.x, n4.y)));
+        const float2 l23 = f2upk(ffma2(
+            a2x2, f2pk(__uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3])),
+            f2pk(n4.z, n4.w)));
+        const float2 l45 = f2upk(ffma2(
+            a2x2, f2pk(__uint_as_float(sv[j + 4]), __uint_as_float(sv[j + 5])),
+            f2pk(m4.x, m4.y)));
+        const float2 l67 = f2upk(ffma2(
+            a2x2, f2pk(__uint_as_float(sv[j + 6]), __uint_as_float(sv[j + 7])),
+            f2pk(m4.z, m4.w)));
+        sv[j] = __float_as_uint(l01.x);
+        sv[j + 1] = __float_as_uint(l01.y);
+        sv[j + 2] = __float_as_uint(l23.x);
+        sv[j + 3] = __float_as_uint(l23.y);
+        sv[j + 4] = __float_as_uint(l45.x);
+        sv[j + 5] = __float_as_uint(l45.y);
+        sv[j + 6] = __float_as_uint(l67.x);
+        sv[j + 7] = __float_as_uint(l67.y);
+        mxa = fmax3(mxa, l01.x, l01.y);
+        mxb = fmax3(mxb, l23.x, l23.y);
+        mxc = fmax3(mxc, l45.x, l45.y);
+        mxd = fmax3(mxd, l67.x, l67.y);
       }
+      const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
       // Lazy rescaling: move this row's reference max only when the max
       // grew by more than 2^8; the warp rescales O if any of its rows moved.
       // (PV_X(t-1) has completed: QK_X(t) ran after it, in order.)
@@ -571,43 +618,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(o_col + c * 32, ov);
         }
       }
-      // Pass 2: P = exp2(logit - m), packed to pairs over the S columns
-      // already read (chunk c of S -> P columns 16c..16c+15); TMEM loads
-      // pipelined as in pass 1.
+      // P = exp2(logit - m) from the registers, packed to pairs and
+      // stored over the S columns (chunk c -> P columns 16c..16c+15).
       const float ref = m_used == kNegInf ? 0.f : m_used;
       const uint64_t negref2 = f2pk(-ref, -ref);
       uint64_t lsum2a = 0, lsum2b = 0;
-      {
-        uint32_t buf[2][32];
-        tmem_ld32u(s_col, buf[0]);
 #pragma unroll
-        for (int c = 0; c < kTileN / 32; ++c) {
-          uint32_t* cur = buf[c & 1];
-          tmem_wait_ld_tied(cur);
-          if (c + 1 < kTileN / 32) tmem_ld32u(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
-          uint32_t pp[16];
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t pp[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 n4 =
-                *reinterpret_cast<const float4*>(nkb + c * 32 + j);
-            const uint64_t b01 = fadd2(f2pk(n4.x, n4.y), negref2);
-            const uint64_t b23 = fadd2(f2pk(n4.z, n4.w), negref2);
-            const float2 x01 = f2upk(ffma2(
-                a2x2, f2pk(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])),
-                b01));
-            const float2 x23 = f2upk(ffma2(
-                a2x2,
-                f2pk(__uint_as_float(cur[j + 2]), __uint_as_float(cur[j + 3])),
-                b23));
-            const float e0 = fast_exp2(x01.x), e1 = fast_exp2(x01.y);
-            const float e2 = fast_exp2(x23.x), e3 = fast_exp2(x23.y);
-            lsum2a = fadd2(lsum2a, f2pk(e0, e1));
-            lsum2b = fadd2(lsum2b, f2pk(e2, e3));
-            pp[j / 2] = pack2<T>(e0, e1);
-            pp[j / 2 + 1] = pack2<T>(e2, e3);
-          }
-          tmem_st16(s_col + c * 16, pp);
+        for (int j = 0; j < 32; j += 4) {
+          const int k = c * 32 + j;
+          const float2 x01 = f2upk(fadd2(
+              f2pk(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1])),
+              negref2));
+          const float2 x23 = f2upk(fadd2(
+              f2pk(__uint_as_float(sv[k + 2]), __uint_as_float(sv[k + 3])),
+              negref2));
+          const float e0 = fast_exp2(x01.x), e1 = fast_exp2(x01.y);
+          const float e2 = fast_exp2(x23.x), e3 = fast_exp2(x23.y);
+          lsum2a = fadd2(lsum2a, f2pk(e0, e1));
+          lsum2b = fadd2(lsum2b, f2pk(e2, e3));
+          pp[j / 2] = pack2<T>(e0, e1);
+          pp[j / 2 + 1] = pack2<T>(e2, e3);
         }
+        tmem_st16(s_col + c * 16, pp);
       }
       const float2 la = f2upk(lsum2a), lb = f2upk(lsum2b);
       const float lsum = (la.x + la.y) + (lb.x + lb.y);
@@ -720,7 +755,15 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
   if (dev < 0 || dev >= 64 || !configured[dev].load()) {
-    cudaError_t err = cudaFuncSetAttribute(
+    // The setmaxnreg split must fit in the registers the block is launched
+    // with; a deficit would leave setmaxnreg.inc waiting forever.
+    cudaFuncAttributes attr;
+    cudaError_t err = cudaFuncGetAttributes(&attr, kern);
+    if (err != cudaSuccess) return err;
+    if (int64_t(attr.numRegs) * kThreads <
+        int64_t(2 * 128) * kSoftmaxRegs + int64_t(128) * kOtherRegs)
+      return cudaErrorInvalidConfiguration;
+    err = cudaFuncSetAttribute(
         kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) configured[dev].store(1);
