@@ -81,13 +81,16 @@ typedef struct {
 #define VECTRA_FLAG_FORCE_GENERIC 0x1u /* the any-shape tiled kernel */
 #define VECTRA_FLAG_FORCE_DECODE  0x2u /* the Nq == 1 streaming kernel */
 #define VECTRA_FLAG_FORCE_TC      0x4u /* the tcgen05/TMEM tensor-core kernel */
+#define VECTRA_FLAG_FORCE_DECODE_MMA 0x8u /* the Nq == 1 tensor-core kernel
+                                              (never chosen automatically) */
 
 /* Kernels (vectra_rbf_select_kernel's result). */
 enum {
   VECTRA_KERNEL_NONE = 0,     /* nothing to launch (an empty problem) */
   VECTRA_KERNEL_GENERIC = 1,  /* rbf_generic: any shape, stride and dtype */
   VECTRA_KERNEL_DECODE = 2,   /* rbf_decode: Nq == 1, bulk-copy streaming */
-  VECTRA_KERNEL_TC = 3        /* rbf_tc: tcgen05 + TMEM, long sequences */
+  VECTRA_KERNEL_TC = 3,       /* rbf_tc: tcgen05 + TMEM, long sequences */
+  VECTRA_KERNEL_DECODE_MMA = 4 /* rbf_decode_mma: Nq == 1, mma.sync dots */
 };
 
 /* Arguments of one forward call.
@@ -116,7 +119,8 @@ VECTRA_API int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* s
  * tile_configs.py:114-133). */
 VECTRA_API int vectra_rbf_select_kernel(const vectra_rbf_args* args);
 
-/* Name of a VECTRA_KERNEL_* value ("generic", "decode", "tc", "none"). */
+/* Name of a VECTRA_KERNEL_* value ("none", "generic", "decode", "tc",
+ * "decode_mma"). */
 VECTRA_API const char* vectra_rbf_kernel_name(int kernel);
 
 /* Message for a status code. */

@@ -42,8 +42,8 @@ def test_status_strings():
     assert _lib.strerror(_lib.ERR_BIAS_QUERY) == (
         'key_bias must be constant across queries')
     assert _lib.strerror(12345) == 'unknown status'
-    assert [_lib.kernel_name(k) for k in range(4)] == [
-        'none', 'generic', 'decode', 'tc']
+    assert [_lib.kernel_name(k) for k in range(5)] == [
+        'none', 'generic', 'decode', 'tc', 'decode_mma']
 
 
 def test_build_info_names_the_architecture():
@@ -91,6 +91,13 @@ def _select(a):
 def test_serving_shape_selects_the_decode_kernel():
     assert _select(_args()) == _lib.KERNEL_DECODE
     assert _select(_args(bias_shape=(4, 1, 1, 64))) == _lib.KERNEL_DECODE
+    assert _select(_args(d=128, dv=128)) == _lib.KERNEL_DECODE
+    assert _select(_args(d=32, dv=32)) == _lib.KERNEL_DECODE
+    # The tensor-core decode kernel takes it only when pinned.
+    assert _select(_args(flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
+        _lib.KERNEL_DECODE_MMA)
+    assert _select(_args(d=128, dv=128, flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
+        _lib.KERNEL_DECODE_MMA)
 
 
 def test_config1_fp32_selects_decode():
@@ -114,6 +121,11 @@ def test_forced_kernels():
     assert _select(_args(flags=_lib.FLAG_FORCE_GENERIC)) == (
         _lib.KERNEL_GENERIC)
     assert _select(_args(nq=2, flags=_lib.FLAG_FORCE_DECODE)) == (
+        _lib.ERR_FORCED)
+    assert _select(_args(nq=2, flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
+        _lib.ERR_FORCED)
+    assert _select(_args(dtype=_lib.F32, d=64, dv=64,
+                         flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
         _lib.ERR_FORCED)
 
 

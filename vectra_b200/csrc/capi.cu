@@ -129,6 +129,12 @@ int select(const RbfProblem& p, uint32_t flags) {
     return decode_supports(p) ? VECTRA_KERNEL_DECODE : VECTRA_ERR_FORCED;
   if (flags & VECTRA_FLAG_FORCE_TC)
     return tc_supports(p) ? VECTRA_KERNEL_TC : VECTRA_ERR_FORCED;
+  if (flags & VECTRA_FLAG_FORCE_DECODE_MMA)
+    return decode_mma_supports(p) ? VECTRA_KERNEL_DECODE_MMA
+                                  : VECTRA_ERR_FORCED;
+  // Nq == 1: the SIMT decode kernel measured faster than the mma.sync one on
+  // every serving shape tried (config 2: 26.3 us against 28.7 us; config 3:
+  // 170 us against 178 us), so the tensor-core decode kernel is opt-in.
   if (decode_supports(p)) return VECTRA_KERNEL_DECODE;
   if (tc_supports(p)) return VECTRA_KERNEL_TC;
   return VECTRA_KERNEL_GENERIC;
@@ -194,6 +200,9 @@ int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* stream) {
     case VECTRA_KERNEL_TC:
       err = launch_tc(p, s);
       break;
+    case VECTRA_KERNEL_DECODE_MMA:
+      err = launch_decode_mma(p, s);
+      break;
     default:
       err = launch_generic(p, s);
       break;
@@ -213,6 +222,8 @@ const char* vectra_rbf_kernel_name(int kernel) {
       return "decode";
     case VECTRA_KERNEL_TC:
       return "tc";
+    case VECTRA_KERNEL_DECODE_MMA:
+      return "decode_mma";
     default:
       return "invalid";
   }

@@ -10,6 +10,7 @@
 // (kernels/vectra_kernels/reference.py:146-152).
 #pragma once
 
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -270,8 +271,18 @@ cudaError_t launch_generic(const RbfProblem& p, cudaStream_t stream);
 cudaError_t launch_decode(const RbfProblem& p, cudaStream_t stream);
 // True when the decode kernel has an instantiation and the layout it needs.
 bool decode_supports(const RbfProblem& p);
+cudaError_t launch_decode_mma(const RbfProblem& p, cudaStream_t stream);
+bool decode_mma_supports(const RbfProblem& p);
 cudaError_t launch_tc(const RbfProblem& p, cudaStream_t stream);
 bool tc_supports(const RbfProblem& p);
+
+// TMA tensor maps (tma_maps.cu). A [B, H, N, D] bf16/f16 view with element
+// strides s (s[3] == 1) as a 4-D map with a box of 64 columns (128 bytes,
+// SWIZZLE_128B) by `box_rows` rows; rows past N read as zeros.
+bool tensor_maps_available();
+bool make_tile_map(CUtensorMap* map, const void* base, int dtype, int64_t B,
+                   int64_t H, int64_t N, int64_t D, const int64_t* s,
+                   int box_rows);
 
 // Streaming-multiprocessor count of the current device (cached).
 int device_sm_count();

@@ -37,8 +37,6 @@
 //  * Epilogue: each softmax warpgroup reads its O from TMEM, divides by the
 //    running sum and stores its rows.
 // Every mbarrier wait is bounded (error word + early exit, no trap).
-#include <cudaTypedefs.h>
-
 #include <atomic>
 #include <mutex>
 #include <type_traits>
@@ -695,55 +693,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side: tensor maps and launch.
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr,
-                                cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-// [B, H, N, D] view with element strides s (s[3] == 1), box 64 x 128.
-bool make_map(CUtensorMap* map, const void* base, int dtype, int64_t B,
-              int64_t H, int64_t N, int64_t D, const int64_t* s) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const int64_t es = 2;
-  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H),
-                        cuuint64_t(B)};
-  cuuint64_t strides[3] = {cuuint64_t(s[2] * es), cuuint64_t(s[1] * es),
-                           cuuint64_t(s[0] * es)};
-  // Broadcast or degenerate strides: give size-1 dimensions a valid stride.
-  if (N == 1) strides[0] = cuuint64_t(D * es + 15) / 16 * 16;
-  if (H == 1) strides[1] = strides[0] * N;
-  if (B == 1) strides[2] = strides[1] * H;
-  cuuint32_t box[4] = {64, cuuint32_t(kTileN), 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUresult r = fn(map,
-                        dtype == VECTRA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        4, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 template <typename T, int D>
 cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
   using Cfg = TcCfg<D>;
   CUtensorMap tq, tk, tv;
-  if (encode_fn() == nullptr) return cudaErrorNotSupported;
-  if (!make_map(&tq, p.q, p.dtype, p.B, p.H, p.Nq, D, p.sq) ||
-      !make_map(&tk, p.k, p.dtype, p.B, p.H, p.Nk, D, p.sk) ||
-      !make_map(&tv, p.v, p.dtype, p.B, p.H, p.Nk, D, p.sv))
+  if (!tensor_maps_available()) return cudaErrorNotSupported;
+  if (!make_tile_map(&tq, p.q, p.dtype, p.B, p.H, p.Nq, D, p.sq, kTileN) ||
+      !make_tile_map(&tk, p.k, p.dtype, p.B, p.H, p.Nk, D, p.sk, kTileN) ||
+      !make_tile_map(&tv, p.v, p.dtype, p.B, p.H, p.Nk, D, p.sv, kTileN))
     return cudaErrorInvalidValue;
   TcParams P;
   P.n_qtiles = static_cast<int>((p.Nq + kTilesQ * kTileM - 1) /
