@@ -165,6 +165,8 @@ def run_reference(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return 0
+    sys.path.insert(0, ROOT)
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
     metric, unit = metric_for(args.config)
     threads = os.cpu_count() or 1
     per_step = max(0.2, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
@@ -180,7 +182,8 @@ def run_reference(args):
         'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
         'dtype': 'f32', 'data': 'synthetic (seeded, BASELINE config shapes)',
-        'config': {'workload': f'config{args.config}', 'device': 'host CPU'},
+        'config': {'workload': workloads.NAMES[args.config],
+                   'device': 'host CPU', 'threads': cores},
         'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
                          'kind': 'port', 'sample': sample},
         'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,

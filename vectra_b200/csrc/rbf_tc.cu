@@ -22,7 +22,7 @@
 //  * warp 8, one lane: TMA producer. Q (both tiles) once, then K and V tiles
 //    of 128 keys into a 2-stage ring (128-byte swizzled, the canonical UMMA
 //    K-major / MN-major layouts) via 4-D tensor maps over [B, H, N, D] with
-//    the caller's strides. No multicast.
+//    the caller's strides; each CTA loads its own tiles.
 //  * warp 9: allocates all 512 TMEM columns (S_A, S_B, O_A, O_B); lane 0
 //    issues the MMAs, ping-ponging the tiles so the tensor core works on
 //    one tile while the other's softmax runs:
@@ -302,7 +302,7 @@ __device__ __forceinline__ void tmem_wait_ld() {
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-// 4-D tiled TMA load (no multicast) completing on `bar`.
+// 4-D tiled TMA load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap,
                                             uint32_t bar, int c0, int c1,
                                             int c2, int c3) {
