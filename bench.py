@@ -59,6 +59,9 @@ def parse_args(argv=None):
     p.add_argument('--impl', default='vectra', choices=('vectra',
                                                          'reference'))
     p.add_argument('--e2e-steps', type=int, default=20)
+    p.add_argument('--graph-calls', type=int, default=0,
+                   help='operator calls per replayed CUDA graph in the timed '
+                        'region (0: a multiple of the input sets, >= 12)')
     p.add_argument('--cpu-seconds', type=float, default=10.0)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--profile', action='store_true',
@@ -317,47 +320,58 @@ def run_vectra(args):
         if i % 64 == 0:
             torch.cuda.synchronize()
 
-    # Timed region: exactly K steps. Each step replays a CUDA graph that
-    # holds one operator call on one of the rotating input sets, so the
-    # host's per-call dispatch never starves the GPU; the region is timed
-    # with CUDA events on the launching stream.
-    graphs = []
+    # Timed region: exactly K steps, one operator call on one batch each,
+    # call t on input set t mod n_sets. The calls are replayed from CUDA
+    # graphs that hold G consecutive calls (G = the smallest multiple of
+    # n_sets that is at least 12), so the host's per-call dispatch never
+    # starves the GPU and consecutive kernels are not separated by graph
+    # launches; a second graph holds the K mod G calls left over. Timed with
+    # CUDA events on the launching stream.
+    per_graph = args.graph_calls or n_sets * -(-12 // n_sets)
+    per_graph = max(1, min(per_graph, args.steps))
+    full, rest = divmod(args.steps, per_graph)
     capture_stream = torch.cuda.Stream(dev)
     capture_stream.wait_stream(stream)
-    launches_per_graph = []
+
+    def capture(n_calls):
+        g = torch.cuda.CUDAGraph()
+        before = vectra_b200.launch_count()
+        with torch.cuda.graph(g, stream=capture_stream):
+            for c in range(n_calls):
+                step(c)
+        return g, vectra_b200.launch_count() - before
+
     with torch.cuda.stream(capture_stream):
         for i in range(n_sets):
             step(i)  # warm the capture stream
         capture_stream.synchronize()
-        for i in range(n_sets):
-            g = torch.cuda.CUDAGraph()
-            before = vectra_b200.launch_count()
-            with torch.cuda.graph(g, stream=capture_stream):
-                step(i)
-            launches_per_graph.append(vectra_b200.launch_count() - before)
-            graphs.append(g)
+        main_graph, main_launches = capture(per_graph)
+        rest_graph, rest_launches = capture(rest) if rest else (None, 0)
     stream.wait_stream(capture_stream)
-    for i in range(n_sets):
-        graphs[i].replay()
+    main_graph.replay()
+    if rest_graph is not None:
+        rest_graph.replay()
     region0 = torch.cuda.Event(enable_timing=True)
     region1 = torch.cuda.Event(enable_timing=True)
     barrier()
     region0.record(stream)
-    for i in range(args.steps):
-        graphs[i % n_sets].replay()
+    for _ in range(full):
+        main_graph.replay()
+    if rest_graph is not None:
+        rest_graph.replay()
     region1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    launches = sum(launches_per_graph[i % n_sets] for i in range(args.steps))
+    launches = full * main_launches + rest_launches
     region_ms = region0.elapsed_time(region1)
-    # Back-to-back replays keep the GPU busy, so the kernel's average launch
+    # Back-to-back kernels keep the GPU busy, so the kernel's average launch
     # duration is the region over K (an upper bound: it includes the small
     # gaps between kernels).
     kernel_ms = region_ms / args.steps
     clocks = sampler.stop()
     slowest_ms = max_over_ranks(region_ms)
     ms_per_step = slowest_ms / args.steps
-    del graphs
+    del main_graph, rest_graph
 
     # End to end through the public API: pinned host inputs copied in,
     # the operator, the result copied out, every step.
@@ -431,6 +445,7 @@ def run_vectra(args):
                 'workload': workloads.NAMES[args.config],
                 'queries_per_gpu': queries, 'global_batch': queries * world,
                 'parallelism': f'batch-sharded x{world}, no collective',
+                'graph_calls': per_graph,
                 'l2': f'{n_sets} rotating input sets of '
                       f'{set_bytes / 1e6:.0f} MB (> L2 {L2_BYTES >> 20} MiB)',
                 'kernel': vectra_b200.kernel_for(*w0.tensors()),

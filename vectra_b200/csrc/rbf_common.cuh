@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "vectra_rbf.h"
 
 namespace vectra {
@@ -264,6 +266,41 @@ __device__ __forceinline__ uint64_t l2_evict_normal_policy() {
   asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;"
                : "=l"(policy));
   return policy;
+}
+
+// Programmatic dependent launch. A kernel launched with launch_pdl may
+// start while the previous kernel in the stream is still running; it calls
+// allow_dependents() early (the next such kernel may then be scheduled as
+// SMs free up) and grid_dependency_wait() before its first global-memory
+// access, which returns once every earlier kernel has completed and its
+// writes are visible. So inputs produced, and buffers read, by the previous
+// kernel are ordered exactly as with a plain launch; only the launch
+// latency and the shared-memory set-up overlap. Without a programmatic
+// dependency both instructions are no-ops.
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+#ifndef VECTRA_PDL
+#define VECTRA_PDL 1  // 0: plain launches (for comparison)
+#endif
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                       size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = VECTRA_PDL ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Kernel launchers (one per translation unit). Each returns a cudaError_t.

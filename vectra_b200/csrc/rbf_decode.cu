@@ -48,8 +48,26 @@
 #ifndef VECTRA_DECODE_MAX_STAGES
 #define VECTRA_DECODE_MAX_STAGES 64
 #endif
-constexpr int kSmallStageBytes = 8192, kSmallStageWarps = 16;
-constexpr int kLargeStageBytes = 16384, kLargeStageWarps = 8;
+#ifndef VECTRA_DECODE_SMALL_BYTES
+#define VECTRA_DECODE_SMALL_BYTES 8192
+#endif
+#ifndef VECTRA_DECODE_SMALL_WARPS
+#define VECTRA_DECODE_SMALL_WARPS 16
+#endif
+#ifndef VECTRA_DECODE_LARGE_BYTES
+#define VECTRA_DECODE_LARGE_BYTES 16384
+#endif
+#ifndef VECTRA_DECODE_LARGE_WARPS
+#define VECTRA_DECODE_LARGE_WARPS 8
+#endif
+// Stages kept in flight beyond one per computing warp.
+#ifndef VECTRA_DECODE_MIN_INFLIGHT
+#define VECTRA_DECODE_MIN_INFLIGHT 6
+#endif
+constexpr int kSmallStageBytes = VECTRA_DECODE_SMALL_BYTES;
+constexpr int kSmallStageWarps = VECTRA_DECODE_SMALL_WARPS;
+constexpr int kLargeStageBytes = VECTRA_DECODE_LARGE_BYTES;
+constexpr int kLargeStageWarps = VECTRA_DECODE_LARGE_WARPS;
 // 1: keys and values are copied with an L2 evict-first policy (they are
 // read exactly once); 0: default L2 policy.
 #ifndef VECTRA_DECODE_L2_EVICT_FIRST
@@ -204,7 +222,10 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
     }
     fence_barrier_init();
   }
+  allow_dependents();
   __syncthreads();
+  // Every global access (inputs, output, error word) comes after this.
+  grid_dependency_wait();
 
   // Copies item i into stage i % ns (the whole warp takes part). The
   // copies are armed by lane kIssueLane, a lane that never stores output:
@@ -508,7 +529,9 @@ struct DecodeLauncher {
     if (ns < 2) return cudaErrorInvalidConfiguration;
     // Keep at least ~6 stages in flight while the other warps compute.
     int warps = WARPS;
-    if (ns - warps < 6) warps = ns - 6 > 4 ? ns - 6 : (ns > 4 ? 4 : ns);
+    constexpr int kInflight = VECTRA_DECODE_MIN_INFLIGHT;
+    if (ns - warps < kInflight)
+      warps = ns - kInflight > 4 ? ns - kInflight : (ns > 4 ? 4 : ns);
     DecodeLaunch L;
     L.ns = ns;
     L.n_planes = static_cast<int>(p.B * p.H);
@@ -532,8 +555,8 @@ struct DecodeLauncher {
       if (err != cudaSuccess) return err;
       if (dev >= 0 && dev < 64) configured[dev].store(1);
     }
-    kern<<<static_cast<unsigned>(blocks), warps * 32, smem, stream>>>(p, L);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)),
+                      dim3(warps * 32), smem, stream, p, L);
   }
 };
 
