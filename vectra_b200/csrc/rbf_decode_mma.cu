@@ -164,7 +164,9 @@ __global__ void __launch_bounds__(32 * kWarps, 1)
     }
     fence_barrier_init();
   }
+  allow_dependents();
   __syncthreads();
+  grid_dependency_wait();  // before any global access
 
   // Copies item i into stage i % ns; lane 31 (which never stores output)
   // arms the copies and then publishes "stage s holds item i".
@@ -448,9 +450,8 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) configured[dev].store(1);
   }
-  kern<<<static_cast<unsigned>(blocks), kWarps * 32, smem, stream>>>(tk, tv,
-                                                                     p, L);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)),
+                    dim3(kWarps * 32), smem, stream, tk, tv, p, L);
 }
 
 bool aligned16(const void* ptr) {

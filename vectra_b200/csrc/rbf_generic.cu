@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(kThreads)
   const T* __restrict__ k = static_cast<const T*>(p.k);
   const T* __restrict__ v = static_cast<const T*>(p.v);
   T* __restrict__ out = static_cast<T*>(p.out);
+  allow_dependents();
+  grid_dependency_wait();  // before any global access
 
   for (int64_t blk = blockIdx.x; blk < n_blocks; blk += gridDim.x) {
     const int64_t plane = blk / n_qtiles;
@@ -167,9 +169,8 @@ cudaError_t launch_generic_t(const RbfProblem& p, cudaStream_t stream) {
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
   const unsigned grid =
       static_cast<unsigned>(n_blocks < cap ? n_blocks : cap);
-  rbf_generic_kernel<T><<<grid, kThreads, smem, stream>>>(p, n_qtiles,
-                                                          n_blocks);
-  return cudaGetLastError();
+  return launch_pdl(rbf_generic_kernel<T>, dim3(grid), dim3(kThreads), smem,
+                    stream, p, n_qtiles, n_blocks);
 }
 
 }  // namespace

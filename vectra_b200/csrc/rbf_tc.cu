@@ -395,9 +395,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
     tmem_relinquish();
   }
+  allow_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dependency_wait();  // before any global access
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
@@ -725,9 +727,8 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) configured[dev].store(1);
   }
-  kern<<<static_cast<unsigned>(blocks), kThreads, Cfg::SMEM_ALLOC, stream>>>(
-      tq, tk, tv, p, P);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(kThreads),
+                    Cfg::SMEM_ALLOC, stream, tq, tk, tv, p, P);
 }
 
 bool aligned16(const void* ptr) {
