@@ -9,6 +9,8 @@ D=64, bf16). With N GPUs (torchrun, one process per GPU) every rank
 processes its own batch of the same size (weak scaling; queries are
 independent, there is no collective on the data path) and the value is the
 total queries of all ranks divided by the slowest rank's device time.
+`--scaling strong` splits one batch of the configured size across the
+ranks instead (contiguous shards of identically seeded data).
 
 Rank 0 prints one JSON line with:
 * value: queries/s (or TFLOP/s for config 4), inputs resident in HBM,
@@ -59,6 +61,9 @@ def parse_args(argv=None):
     p.add_argument('--impl', default='vectra', choices=('vectra',
                                                          'reference'))
     p.add_argument('--e2e-steps', type=int, default=20)
+    p.add_argument('--scaling', default='weak', choices=('weak', 'strong'),
+                   help='weak: each GPU runs the configured batch; strong: '
+                        'the GPUs split one configured batch')
     p.add_argument('--graph-calls', type=int, default=0,
                    help='operator calls per replayed CUDA graph in the timed '
                         'region (0: a multiple of the input sets, >= 12)')
@@ -192,7 +197,7 @@ def run_reference(args):
         'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -255,6 +260,7 @@ def run_vectra(args):
     import torch.distributed as dist  # pylint: disable=import-outside-toplevel
     sys.path.insert(0, ROOT)
     import vectra_b200  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
     from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
 
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -274,20 +280,33 @@ def run_vectra(args):
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        if distributed:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(x, device=dev)
 
-    # Weak scaling: every rank has its own batch of the configured size.
-    sets = []
-    w0 = workloads.make(args.config, device=dev, seed=1000 * rank)
-    set_bytes = workloads.dense_bytes(w0)
-    n_sets = max(1, min(8, -(-3 * L2_BYTES // set_bytes)))
-    sets.append(w0)
-    for i in range(1, n_sets):
-        sets.append(workloads.make(args.config, device=dev,
-                                   seed=1000 * rank + i))
+    # Weak scaling (default): every rank has its own batch of the configured
+    # size. Strong scaling: every rank generates the same global batch and
+    # keeps its contiguous shard (sharding.shard_range), so the ranks
+    # together do the 1-GPU job.
+    strong = args.scaling == 'strong'
+
+    def make_set(i):
+        if not strong:
+            return workloads.make(args.config, device=dev,
+                                  seed=1000 * rank + i)
+        full = workloads.make(args.config, device=dev, seed=i)
+        lo, hi = sharding.shard_range(full.batch, world, rank)
+        part = full.slice(lo, hi)
+        return workloads.Workload(
+            part.config, part.dtype,
+            *(None if t is None else t.clone()
+              for t in (part.q, part.k, part.v, part.scale, part.key_bias,
+                        part.lengths)))
+
+    w0 = make_set(0)
+    global_batch = (workloads.SHAPES[args.config][0] if strong
+                    else w0.batch * world)
+    set_bytes = max(1, workloads.dense_bytes(w0))
+    n_sets = max(1, min(32 if strong else 8, -(-3 * L2_BYTES // set_bytes)))
+    sets = [w0] + [make_set(i) for i in range(1, n_sets)]
     alg_bytes = workloads.algorithmic_bytes(w0)
     flops = workloads.algorithmic_flops(w0)
     queries = w0.batch
@@ -409,16 +428,17 @@ def run_vectra(args):
     metric, unit = metric_for(args.config)
     hbm, tflops_peak, peak_kind = peaks()
     if args.config == 4:
-        value = world * flops / (ms_per_step * 1e-3) / 1e12
-        e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
+        job_flops = flops * global_batch / w0.batch
+        value = job_flops / (ms_per_step * 1e-3) / 1e12
+        e2e_value = job_flops / (e2e_ms * 1e-3) / 1e12
         achieved = flops / (kernel_ms * 1e-3) / 1e12
         roof = {'bound': 'tensor', 'achieved': achieved,
                 'peak': tflops_peak, 'unit': 'TFLOP/s',
                 'frac': achieved / tflops_peak, 'traffic': ncu_traffic(4),
                 'peak_kind': f'bf16 dense, {peak_kind} (burst)'}
     else:
-        value = world * queries / (ms_per_step * 1e-3)
-        e2e_value = world * queries / (e2e_ms * 1e-3)
+        value = global_batch / (ms_per_step * 1e-3)
+        e2e_value = global_batch / (e2e_ms * 1e-3)
         achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
         roof = {'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
                 'unit': 'GB/s', 'frac': achieved / hbm,
@@ -437,14 +457,15 @@ def run_vectra(args):
             'metric': metric, 'value': value, 'unit': unit,
             'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
             'ms_per_step': ms_per_step, 'higher_is_better': True,
-            'scaling': 'weak', 'vs_baseline': None,
+            'scaling': args.scaling, 'vs_baseline': None,
             'dtype': w0.dtype,
             'data': 'synthetic (seeded; BASELINE config shapes and '
                     'distributions)',
             'config': {
                 'workload': workloads.NAMES[args.config],
-                'queries_per_gpu': queries, 'global_batch': queries * world,
-                'parallelism': f'batch-sharded x{world}, no collective',
+                'queries_per_gpu': queries, 'global_batch': global_batch,
+                'parallelism': f'batch-sharded x{world} ({args.scaling} '
+                               'scaling), no collective',
                 'graph_calls': per_graph,
                 'l2': f'{n_sets} rotating input sets of '
                       f'{set_bytes / 1e6:.0f} MB (> L2 {L2_BYTES >> 20} MiB)',
@@ -459,17 +480,43 @@ def run_vectra(args):
             'cpu_baseline': cpu,
             'clocks': clocks,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if distributed:
         dist.destroy_process_group()
     return 0
 
 
+# The JSON line goes to the process's original standard output; while the
+# benchmark runs, file descriptor 1 points at standard error, so that what
+# libraries print there (NCCL's version banner, for one) cannot come before
+# or between the lines a driver parses.
+_RESULT_OUT = None
+
+
+def emit(line):
+    out = _RESULT_OUT or sys.stdout
+    out.write(json.dumps(line) + '\n')
+    out.flush()
+
+
 def main(argv=None):
+    global _RESULT_OUT  # pylint: disable=global-statement
     args = parse_args(argv)
-    if args.impl == 'reference':
-        return run_reference(args)
-    return run_vectra(args)
+    sys.stdout.flush()
+    saved = os.dup(1)
+    try:
+        _RESULT_OUT = os.fdopen(os.dup(saved), 'w')
+        os.dup2(2, 1)
+        if args.impl == 'reference':
+            return run_reference(args)
+        return run_vectra(args)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+        if _RESULT_OUT is not None:
+            _RESULT_OUT.close()
+            _RESULT_OUT = None
 
 
 if __name__ == '__main__':
