@@ -99,7 +99,8 @@ def peaks():
 
 def ncu_traffic(config):
     """DRAM bytes per launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, 'profiles', f'ncu_config{config}.txt')
+    kernel = 'rbf_tc' if config == 4 else 'rbf_decode'
+    path = os.path.join(ROOT, 'profiles', f'{kernel}_config{config}.txt')
     try:
         with open(path, encoding='utf-8') as f:
             for line in f:
