@@ -39,13 +39,16 @@ DECODE_SHAPES = [
 ]
 
 
-def _kernels_for(q_shape, d, dv, dtype):
+def _kernels_for(q_shape, d, dv, dtype, nk):
     kernels = ['auto', 'generic']
     if q_shape[2] == 1 and d == dv and (
             d in (32, 64, 128) if dtype != 'f32' else d in (32, 64)):
         kernels.append('decode')
     if q_shape[2] == 1 and d == dv and d in (64, 128) and dtype != 'f32':
         kernels.append('decode_mma')
+    if (q_shape[2] >= 2 and nk <= 128 and d == dv and d in (32, 64)
+            and dtype != 'f32'):
+        kernels.append('small')
     return kernels
 
 
@@ -61,7 +64,8 @@ def _case_tol(name, dtype, v):
 def test_matches_reference_golden_vectors(name):
     c = golden.load(name)
     q, k, v = c['q'], c['k'], c['v']
-    for kernel in _kernels_for(q.shape, q.shape[3], v.shape[3], c['dtype']):
+    for kernel in _kernels_for(q.shape, q.shape[3], v.shape[3], c['dtype'],
+                               k.shape[2]):
         out = helpers.run(q, k, v, c['scale'], c['bias'], c['dtype'],
                           kernel=kernel)
         rtol, atol = _case_tol(name, c['dtype'], v)
@@ -73,7 +77,7 @@ def test_matches_reference_golden_vectors(name):
 @pytest.mark.parametrize('with_bias', [False, True])
 def test_matches_float64_oracle(shape, dtype, with_bias):
     q, k, v, scale, bias = helpers.parity_inputs(shape, dtype, 0, with_bias)
-    for kernel in _kernels_for(q.shape, shape[4], shape[5], dtype):
+    for kernel in _kernels_for(q.shape, shape[4], shape[5], dtype, shape[3]):
         out = helpers.run(q, k, v, scale, bias, dtype, kernel=kernel)
         helpers.check_reference_tol(out, q, k, v, scale, bias, dtype)
         helpers.check_baseline_tol(out, q, k, v, scale, bias, dtype)

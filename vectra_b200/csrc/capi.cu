@@ -6,7 +6,7 @@
 // left-padded to rank 4, constant across queries, broadcast over batch and
 // heads. Unlike the reference it makes no device copies of scale or bias
 // (kernels read them in their own dtype through broadcast strides), computes
-// no separate norm pass, and picks one of three kernels.
+// no separate norm pass, and picks the kernel for the shape (select()).
 #include <atomic>
 #include <cstdio>
 #include <mutex>
@@ -132,11 +132,14 @@ int select(const RbfProblem& p, uint32_t flags) {
   if (flags & VECTRA_FLAG_FORCE_DECODE_MMA)
     return decode_mma_supports(p) ? VECTRA_KERNEL_DECODE_MMA
                                   : VECTRA_ERR_FORCED;
+  if (flags & VECTRA_FLAG_FORCE_SMALL)
+    return small_supports(p) ? VECTRA_KERNEL_SMALL : VECTRA_ERR_FORCED;
   // Nq == 1: the SIMT decode kernel measured faster than the mma.sync one on
   // every serving shape tried (config 2: 26.3 us against 28.7 us; config 3:
   // 170 us against 178 us), so the tensor-core decode kernel is opt-in.
   if (decode_supports(p)) return VECTRA_KERNEL_DECODE;
   if (tc_supports(p)) return VECTRA_KERNEL_TC;
+  if (small_supports(p)) return VECTRA_KERNEL_SMALL;
   return VECTRA_KERNEL_GENERIC;
 }
 
@@ -203,6 +206,9 @@ int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* stream) {
     case VECTRA_KERNEL_DECODE_MMA:
       err = launch_decode_mma(p, s);
       break;
+    case VECTRA_KERNEL_SMALL:
+      err = launch_small(p, s);
+      break;
     default:
       err = launch_generic(p, s);
       break;
@@ -224,6 +230,8 @@ const char* vectra_rbf_kernel_name(int kernel) {
       return "tc";
     case VECTRA_KERNEL_DECODE_MMA:
       return "decode_mma";
+    case VECTRA_KERNEL_SMALL:
+      return "small";
     default:
       return "invalid";
   }

@@ -312,14 +312,18 @@ cudaError_t launch_decode_mma(const RbfProblem& p, cudaStream_t stream);
 bool decode_mma_supports(const RbfProblem& p);
 cudaError_t launch_tc(const RbfProblem& p, cudaStream_t stream);
 bool tc_supports(const RbfProblem& p);
+cudaError_t launch_small(const RbfProblem& p, cudaStream_t stream);
+bool small_supports(const RbfProblem& p);
 
 // TMA tensor maps (tma_maps.cu). A [B, H, N, D] bf16/f16 view with element
-// strides s (s[3] == 1) as a 4-D map with a box of 64 columns (128 bytes,
-// SWIZZLE_128B) by `box_rows` rows; rows past N read as zeros.
+// strides s (s[3] == 1) as a 4-D map with a box of `box_cols` columns by
+// `box_rows` rows, swizzled over the box's row (box_cols 64: 128 bytes,
+// SWIZZLE_128B; 32: SWIZZLE_64B; 16: SWIZZLE_32B); rows past N and columns
+// past D read as zeros.
 bool tensor_maps_available();
 bool make_tile_map(CUtensorMap* map, const void* base, int dtype, int64_t B,
                    int64_t H, int64_t N, int64_t D, const int64_t* s,
-                   int box_rows);
+                   int box_rows, int box_cols = 64);
 
 // Streaming-multiprocessor count of the current device (cached).
 int device_sm_count();

@@ -28,7 +28,7 @@ bool tensor_maps_available() { return encode_fn() != nullptr; }
 
 bool make_tile_map(CUtensorMap* map, const void* base, int dtype, int64_t B,
                    int64_t H, int64_t N, int64_t D, const int64_t* s,
-                   int box_rows) {
+                   int box_rows, int box_cols) {
   auto fn = encode_fn();
   if (!fn) return false;
   const int64_t es = 2;
@@ -40,14 +40,20 @@ bool make_tile_map(CUtensorMap* map, const void* base, int dtype, int64_t B,
   if (N == 1) strides[0] = cuuint64_t(D * es + 15) / 16 * 16;
   if (H == 1) strides[1] = strides[0] * N;
   if (B == 1) strides[2] = strides[1] * H;
-  cuuint32_t box[4] = {64, cuuint32_t(box_rows), 1, 1};
+  // The swizzle span is the box's row: 128, 64 or 32 bytes.
+  const int row_bytes = box_cols * int(es);
+  if (row_bytes != 128 && row_bytes != 64 && row_bytes != 32) return false;
+  const CUtensorMapSwizzle swizzle =
+      row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                       : (row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                          : CU_TENSOR_MAP_SWIZZLE_32B);
+  cuuint32_t box[4] = {cuuint32_t(box_cols), cuuint32_t(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(map,
                         dtype == VECTRA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                         4, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

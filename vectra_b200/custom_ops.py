@@ -72,13 +72,14 @@ def rbf_attention(q, k, v, scale, key_bias=None) -> torch.Tensor:
 KERNELS = {'generic': _lib.FLAG_FORCE_GENERIC,
            'decode': _lib.FLAG_FORCE_DECODE,
            'decode_mma': _lib.FLAG_FORCE_DECODE_MMA,
-           'tc': _lib.FLAG_FORCE_TC}
+           'tc': _lib.FLAG_FORCE_TC,
+           'small': _lib.FLAG_FORCE_SMALL}
 
 
 def rbf_attention_with_kernel(q, k, v, scale, key_bias=None,
                               kernel: str = 'auto') -> torch.Tensor:
     """The same operator with the kernel pinned ('generic', 'decode',
-    'decode_mma', 'tc').
+    'decode_mma', 'tc', 'small').
 
     Raises ValueError when the pinned kernel cannot run the problem.
     """
@@ -104,8 +105,8 @@ def _describe(t):
 
 def kernel_for(q, k, v, scale, key_bias=None, kernel: str = 'auto') -> str:
     """Name of the kernel the operator launches for these tensors
-    ('decode', 'decode_mma', 'tc', 'generic' or 'none'); raises ValueError
-    when the arguments are invalid. Launches nothing."""
+    ('decode', 'decode_mma', 'tc', 'small', 'generic' or 'none'); raises
+    ValueError when the arguments are invalid. Launches nothing."""
     import ctypes  # pylint: disable=import-outside-toplevel
     a = _lib.Args()
     a.q, a.k, a.v = _describe(q), _describe(k), _describe(v)
