@@ -474,7 +474,9 @@ def run_vectra(args):
             },
             'e2e': {'value': e2e_value, 'unit': unit,
                     'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
-                    'steps': e2e_steps},
+                    'steps': e2e_steps,
+                    # what bounds it: the host->device copy of the inputs
+                    'h2d_gbs': h2d / (e2e_ms * 1e-3) / 1e9},
             'gpu_launches': launches,
             'kernel_ms_per_launch': kernel_ms,
             'roofline': roof,
