@@ -126,10 +126,24 @@ def cpu_sample(config, n_queries, seed=1):
     return w, tensors
 
 
-def time_cpu(config, seconds, threads):
+def cpu_model():
+    """The host CPU's model name (Linux), for the CPU baseline's record."""
+    try:
+        with open('/proc/cpuinfo', encoding='utf-8') as f:
+            for line in f:
+                if line.startswith('model name'):
+                    return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
+def time_cpu(config, seconds, threads, formulation='matmul'):
     """Queries/s (or TFLOP/s) of the oracle's port of the operator's CPU
-    implementation on `threads` host threads, over a bounded sample for
-    about `seconds`."""
+    implementation (formulation 'matmul', reference.matmul_rbf_attention,
+    the default impl of vectra::rbf_attention) or of the eager chain
+    ('eager', reference.eager_rbf_attention, north_star's CPU path) on
+    `threads` host threads, over a bounded sample for about `seconds`."""
     sys.path.insert(0, ROOT)
     from oracle import rbf_oracle  # pylint: disable=import-outside-toplevel
     from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
@@ -152,9 +166,12 @@ def time_cpu(config, seconds, threads):
     chunks = np.array_split(np.arange(q.shape[0]), threads)
     chunks = [c for c in chunks if len(c)]
 
+    fn = (rbf_oracle.eager_rbf_attention if formulation == 'eager'
+          else rbf_oracle.matmul_rbf_attention)
+
     def work(idx):
         sq, sk, sv, ss, sb = rbf_oracle.sample_planes(q, k, v, s, b, idx)
-        rbf_oracle.matmul_rbf_attention(sq, sk, sv, ss, sb)
+        fn(sq, sk, sv, ss, sb)
 
     with concurrent.futures.ThreadPoolExecutor(len(chunks)) as pool:
         list(pool.map(work, chunks))  # warm-up
@@ -165,9 +182,10 @@ def time_cpu(config, seconds, threads):
             n += 1
         dt = time.perf_counter() - t0
     del workloads
+    what = ('eager-chain port' if formulation == 'eager'
+            else 'matmul port (the op CPU impl)')
     return (n * q.shape[0] / dt, 'queries/s', len(chunks),
-            f'matmul port (the op CPU impl), {q.shape[0]} queries x {n} '
-            'repeats')
+            f'{what}, {q.shape[0]} queries x {n} repeats')
 
 
 def run_reference(args):
@@ -194,7 +212,8 @@ def run_reference(args):
         'config': {'workload': workloads.NAMES[args.config],
                    'device': 'host CPU', 'threads': cores},
         'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
-                         'kind': 'port', 'sample': sample},
+                         'kind': 'port', 'sample': sample,
+                         'cpu_model': cpu_model()},
         'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     }
@@ -452,7 +471,11 @@ def run_vectra(args):
         v, u, cores, sample = time_cpu(args.config, args.cpu_seconds,
                                        os.cpu_count() or 1)
         cpu = {'value': v, 'unit': u, 'cores': cores, 'kind': 'port',
-               'sample': sample}
+               'sample': sample, 'cpu_model': cpu_model()}
+        if args.config != 4:
+            ev, _, _, esample = time_cpu(args.config, args.cpu_seconds / 2,
+                                         os.cpu_count() or 1, 'eager')
+            cpu['eager'] = {'value': ev, 'unit': u, 'sample': esample}
     if rank == 0:
         line = {
             'metric': metric, 'value': value, 'unit': unit,
