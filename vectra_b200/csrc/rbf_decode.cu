@@ -18,9 +18,10 @@
 //    mbarrier) and the consumer first waits for that word to name its
 //    item (acquire), then on the mbarrier parity.
 //  * Key chunks whose bias is -inf are not fetched: the issuing warp reads
-//    the bias first and copies only rows [lo, hi] of the chunk that hold a
+//    the bias first (loaded one item ahead, so the latency overlaps the
+//    current item) and copies only rows [lo, hi] of the chunk that hold a
 //    finite bias (the variable-comparable-count config reads ~half the
-//    bytes).
+//    bytes); a chunk with no finite bias is not computed either.
 //  * Distances: lane j owns keys j, j+32, ... and forms sum_d (q_d - k_d)^2
 //    from its own key row, with packed f32x2 subtract/FMA (two elements per
 //    instruction) into four independent accumulators. Lanes walk the row's
@@ -42,9 +43,12 @@
 // Stage geometry. A stage holds one work item: the q row plus KC key and
 // value rows. Two profiles, picked per problem: small stages (about 8 KB,
 // 16 warps) when a plane has at most two chunks of them, else large stages
-// (about 16 KB, 8 warps), so long key lists take fewer, larger items.
+// (about 16 KB, 11 warps), so long key lists take fewer, larger items.
 // A block holds as many stages as fit in 227 KB (at most
-// VECTRA_DECODE_MAX_STAGES); warps are trimmed so about six stay in flight.
+// VECTRA_DECODE_MAX_STAGES); warps are trimmed so that at least
+// VECTRA_DECODE_MIN_INFLIGHT stages stay in flight beyond one per warp.
+// (Measured on the masked config 3, 13 large stages: 11 warps with 2 spare
+// 150.6 us; 7 warps with 6 spare 168.2 us; 13 warps with none 159.6 us.)
 #ifndef VECTRA_DECODE_MAX_STAGES
 #define VECTRA_DECODE_MAX_STAGES 64
 #endif
@@ -58,16 +62,20 @@
 #define VECTRA_DECODE_LARGE_BYTES 16384
 #endif
 #ifndef VECTRA_DECODE_LARGE_WARPS
-#define VECTRA_DECODE_LARGE_WARPS 8
+#define VECTRA_DECODE_LARGE_WARPS 11
 #endif
 // Stages kept in flight beyond one per computing warp.
 #ifndef VECTRA_DECODE_MIN_INFLIGHT
-#define VECTRA_DECODE_MIN_INFLIGHT 6
+#define VECTRA_DECODE_MIN_INFLIGHT 2
 #endif
 constexpr int kSmallStageBytes = VECTRA_DECODE_SMALL_BYTES;
 constexpr int kSmallStageWarps = VECTRA_DECODE_SMALL_WARPS;
 constexpr int kLargeStageBytes = VECTRA_DECODE_LARGE_BYTES;
 constexpr int kLargeStageWarps = VECTRA_DECODE_LARGE_WARPS;
+// 1: a chunk whose keys are all masked is not computed (it changes nothing).
+#ifndef VECTRA_DECODE_SKIP_EMPTY
+#define VECTRA_DECODE_SKIP_EMPTY 1
+#endif
 // 1: keys and values are copied with an L2 evict-first policy (they are
 // read exactly once); 0: default L2 policy.
 #ifndef VECTRA_DECODE_L2_EVICT_FIRST
@@ -176,7 +184,9 @@ struct DecodeLaunch {
   int v_contig;
 };
 
-template <typename T, int D, int DV, int KC, int WARPS>
+// BIAS: the problem has a key bias (compiled separately, so the no-bias
+// serving path carries none of the mask handling).
+template <typename T, int D, int DV, int KC, int WARPS, bool BIAS>
 __global__ void __launch_bounds__(32 * WARPS, 1)
     rbf_decode_kernel(RbfProblem p, DecodeLaunch L) {
   using Cfg = DecodeCfg<T, D, DV, KC>;
@@ -202,7 +212,7 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
   const T* __restrict__ gk = static_cast<const T*>(p.k);
   const T* __restrict__ gv = static_cast<const T*>(p.v);
   T* __restrict__ gout = static_cast<T*>(p.out);
-  const bool has_bias = p.bias != nullptr;
+  constexpr bool has_bias = BIAS;
   const uint64_t stream_policy = VECTRA_DECODE_L2_EVICT_FIRST
                                      ? l2_evict_first_policy()
                                      : l2_evict_normal_policy();
@@ -232,7 +242,22 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
   // the release ordering of mbarrier.arrive / st.release then has no
   // pending global store of this lane to wait for.
   constexpr int kIssueLane = 31;
-  auto issue = [&](int i) {
+  // The bias of item i's keys in the exp2 domain (lane j: keys j, j + 32,
+  // ...; -inf past the last key), loaded one item ahead of its issue so the
+  // global-load latency overlaps the current item's compute.
+  auto load_item_bias = [&](int i, float (&bvs)[KPL]) {
+    const int g = i / nchunks, chunk = i - g * nchunks;
+    const int plane = int(blockIdx.x) + g * int(gridDim.x);
+    const int b = plane / L.H, h = plane - b * L.H;
+    const int kbase = chunk * KC;
+    const int cnt = min(KC, nk - kbase);
+#pragma unroll
+    for (int t = 0; t < KPL; ++t) {
+      const int j = lane + 32 * t;
+      bvs[t] = j < cnt ? load_bias(p, b, h, kbase + j) * kLog2e : kNegInf;
+    }
+  };
+  auto issue = [&](int i, const float (&bvs)[KPL]) {
     const int g = i / nchunks, chunk = i - g * nchunks;
     const int s = i % ns;
     const int plane = int(blockIdx.x) + g * int(gridDim.x);
@@ -246,8 +271,7 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
 #pragma unroll
       for (int t = 0; t < KPL; ++t) {
         const int j = lane + 32 * t;
-        const float bv =
-            j < cnt ? load_bias(p, b, h, kbase + j) * kLog2e : kNegInf;
+        const float bv = bvs[t];
         meta_bias[s * KC + j] = bv;
         const unsigned live = __ballot_sync(0xffffffffu, bv != kNegInf);
         if (live) {
@@ -297,7 +321,13 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
   };
 
   // Prologue: the first ns items, spread over the warps.
-  for (int i = warp; i < ns && i < n_items; i += W) issue(i);
+  for (int i = warp; i < ns && i < n_items; i += W) {
+    float bvs[KPL];
+#pragma unroll
+    for (int t = 0; t < KPL; ++t) bvs[t] = 0.f;
+    if (has_bias) load_item_bias(i, bvs);
+    issue(i, bvs);
+  }
 
   const int rot = lane / Cfg::ROT_DIV;
   const int vrow = lane / CV;        // value row within a warp step
@@ -315,6 +345,11 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
     for (int chunk = 0; chunk < nchunks; ++chunk) {
       const int i = g * nchunks + chunk;
       const int s = i % ns;
+      const bool refill = i + ns < n_items;
+      float next_bias[KPL];
+#pragma unroll
+      for (int t = 0; t < KPL; ++t) next_bias[t] = 0.f;
+      if (has_bias && refill) load_item_bias(i + ns, next_bias);
       // First: stage s has been armed for item i (not still an earlier
       // item); then: item i's bytes have landed.
       if (!wait_smem_equals(&meta_rng[4 * s + 2], i, p.err) ||
@@ -336,6 +371,9 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
         __syncwarp();
       }
 
+      // A chunk whose keys are all masked changes neither m, l nor acc (its
+      // weights are 0 and its max is -inf), so it is skipped.
+      if (!VECTRA_DECODE_SKIP_EMPTY || lo <= hi) {
       // Squared distances: four partial accumulators (float pairs) per key.
       uint64_t dacc[KPL][4];
 #pragma unroll
@@ -475,8 +513,9 @@ __global__ void __launch_bounds__(32 * WARPS, 1)
         const float2 a = upk(acc[e]), bb = upk(acc_b[e]);
         acc[e] = pk(a.x + bb.x, a.y + bb.y);
       }
+      }
       __syncwarp();  // every lane is done with stage s and pvals
-      if (i + ns < n_items) issue(i + ns);
+      if (refill) issue(i + ns, next_bias);
     }
 
     // Sum the row groups, normalise, store 16 bytes per lane of group 0.
@@ -527,7 +566,7 @@ struct DecodeLauncher {
         (Cfg::STAGE_STRIDE + Cfg::STAGE_META));
     if (ns > VECTRA_DECODE_MAX_STAGES) ns = VECTRA_DECODE_MAX_STAGES;
     if (ns < 2) return cudaErrorInvalidConfiguration;
-    // Keep at least ~6 stages in flight while the other warps compute.
+    // Keep at least kInflight stages in flight beyond the computing warps.
     int warps = WARPS;
     constexpr int kInflight = VECTRA_DECODE_MIN_INFLIGHT;
     if (ns - warps < kInflight)
@@ -543,17 +582,28 @@ struct DecodeLauncher {
     const int64_t cap = device_sm_count();
     if (blocks > cap) blocks = cap;
     const size_t smem = Cfg::block_bytes(ns, warps);
-    auto kern = rbf_decode_kernel<T, D, DV, KC, WARPS>;
-    // The shared-memory attribute is set once per device.
-    static std::atomic<int> configured[64];
+    if (p.bias != nullptr)
+      return run(rbf_decode_kernel<T, D, DV, KC, WARPS, true>, p, L, blocks,
+                 warps, smem, stream);
+    return run(rbf_decode_kernel<T, D, DV, KC, WARPS, false>, p, L, blocks,
+               warps, smem, stream);
+  }
+
+  template <typename Kernel>
+  static cudaError_t run(Kernel kern, const RbfProblem& p,
+                         const DecodeLaunch& L, int64_t blocks, int warps,
+                         size_t smem, cudaStream_t stream) {
+    // The shared-memory attribute is set once per device and kernel.
+    static std::atomic<int> configured[2][64];
+    const int variant = p.bias != nullptr ? 1 : 0;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
-    if (dev < 0 || dev >= 64 || !configured[dev].load()) {
+    if (dev < 0 || dev >= 64 || !configured[variant][dev].load()) {
       cudaError_t err = cudaFuncSetAttribute(
           kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
           static_cast<int>(smem));
       if (err != cudaSuccess) return err;
-      if (dev >= 0 && dev < 64) configured[dev].store(1);
+      if (dev >= 0 && dev < 64) configured[variant][dev].store(1);
     }
     return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)),
                       dim3(warps * 32), smem, stream, p, L);

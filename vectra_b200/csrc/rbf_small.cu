@@ -39,7 +39,11 @@
 namespace vectra {
 namespace {
 
-constexpr int kStages = 3;
+// Stages of the ring (each one item: Q block, K and V of a plane).
+#ifndef VECTRA_SMALL_STAGES
+#define VECTRA_SMALL_STAGES 3
+#endif
+constexpr int kStages = VECTRA_SMALL_STAGES;
 
 struct SmallLaunch {
   int qr;           // queries per item (16 W)
