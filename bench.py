@@ -57,7 +57,8 @@ def parse_args(argv=None):
     p.add_argument('--gpus', type=int, default=1)
     p.add_argument('--steps', type=int, default=2000)
     p.add_argument('--warmup', type=int, default=20)
-    p.add_argument('--config', type=int, default=2, choices=(1, 2, 3, 4))
+    p.add_argument('--config', type=int, default=2,
+                   choices=(1, 2, 3, 4, 5))
     p.add_argument('--impl', default='vectra', choices=('vectra',
                                                          'reference'))
     p.add_argument('--e2e-steps', type=int, default=20)
@@ -80,6 +81,9 @@ def parse_args(argv=None):
 # ---------------------------------------------------------------------------
 
 def metric_for(config):
+    if config == 5:
+        return ('RBF-attn compiled-model site targets/s (B=1024 N=65 H=8 '
+                'D=32 bf16, strided q/k/v)', 'targets/s')
     if config == 4:
         return ('RBF-attn TFLOP/s, long sequences (B=16 H=16 L=4096 D=128 '
                 'bf16)', 'TFLOP/s')
@@ -99,7 +103,7 @@ def peaks():
 
 def ncu_traffic(config):
     """DRAM bytes per launch from the committed ncu summary, if any."""
-    kernel = 'rbf_tc' if config == 4 else 'rbf_decode'
+    kernel = {4: 'rbf_tc', 5: 'rbf_small'}.get(config, 'rbf_decode')
     path = os.path.join(ROOT, 'profiles', f'{kernel}_config{config}.txt')
     try:
         with open(path, encoding='utf-8') as f:
@@ -161,7 +165,7 @@ def time_cpu(config, seconds, threads, formulation='matmul'):
         dt = time.perf_counter() - t0
         return (n * flops / dt / 1e12, 'TFLOP/s', 1,
                 'matmul port, 1 plane x 256 queries x 4096 keys')
-    sample = 256 if config != 1 else 8
+    sample = {1: 8, 5: 32}.get(config, 256)
     w, (q, k, v, s, b) = cpu_sample(config, sample)
     chunks = np.array_split(np.arange(q.shape[0]), threads)
     chunks = [c for c in chunks if len(c)]
@@ -184,8 +188,8 @@ def time_cpu(config, seconds, threads, formulation='matmul'):
     del workloads
     what = ('eager-chain port' if formulation == 'eager'
             else 'matmul port (the op CPU impl)')
-    return (n * q.shape[0] / dt, 'queries/s', len(chunks),
-            f'{what}, {q.shape[0]} queries x {n} repeats')
+    return (n * q.shape[0] / dt, metric_for(config)[1], len(chunks),
+            f'{what}, {q.shape[0]} batch rows x {n} repeats')
 
 
 def run_reference(args):

@@ -1,4 +1,5 @@
-"""BASELINE configs 1-4 at their full sizes (B200 only).
+"""BASELINE configs 1-4 and the config-5 attention site at their full sizes
+(B200 only).
 
 The oracle cannot finish a full batch quickly, so each config is checked
 on seeded batch rows against the eager fp32 oracle (BASELINE's gate), and
@@ -44,7 +45,7 @@ def _convexity(out, v, bias):
     assert bool(((o <= vmax + slack) & (o >= vmin - slack)).all())
 
 
-@pytest.mark.parametrize('config', [1, 2, 3])
+@pytest.mark.parametrize('config', [1, 2, 3, 5])
 def test_serving_configs_full_size(config):
     inp = workloads.make(config, device='cuda', seed=0)
     out = vectra_b200.rbf_attention(inp.q, inp.k, inp.v, inp.scale,

@@ -16,6 +16,13 @@ config descriptions instead, with fixed seeds:
    v ~ N(0,1)/sqrt(D); gamma_h ~ U(0.1, 2.0).
 4. Long sequences: B=16, H=16, Lq=Lk=4096, D=128, bf16;
    q,k,v ~ N(0,1)/sqrt(D); gamma_h ~ U(0.01, 0.2); no mask.
+5. One attention site of the compiled price model (
+   batch 1024 targets, 64 comparables, d_model 256, 8 heads of D=32, bf16):
+   q, k, v are head-transposed views of one [B, N=65, 3, H, D] projection
+   (row stride 3*H*D, the layout the compile pass hands the operator),
+   projection values ~ N(0,1)/sqrt(D); the coefficient 1/(2 sigma_h^2) with
+   log sigma_h ~ N(0.7, 0.3); a [B,1,1,N] bf16 key bias of zeros (every
+   comparable valid, as BASELINE states).
 """
 
 import dataclasses
@@ -30,12 +37,14 @@ SHAPES = {  # B, H, Nq, Nk, D, dtype
     2: (1024, 8, 1, 64, 64, 'bf16'),
     3: (4096, 8, 1, 128, 64, 'bf16'),
     4: (16, 16, 4096, 4096, 128, 'bf16'),
+    5: (1024, 8, 65, 65, 32, 'bf16'),
 }
 NAMES = {
     1: 'config1 B=8 H=4 Lq=1 Lk=16 D=32 fp32',
     2: 'serving B=1024 H=8 Lq=1 Lk=64 D=64 bf16',
     3: 'variable-count B=4096 H=8 Lq=1 Lk_max=128 D=64 bf16 padding bias',
     4: 'long B=16 H=16 Lq=Lk=4096 D=128 bf16',
+    5: 'compiled-model attention site B=1024 N=65 H=8 D=32 bf16 strided',
 }
 
 
@@ -111,6 +120,13 @@ def make(config: int, device='cuda', seed: int = 0,
         valid = torch.arange(nk, device=device)[None, :] < lengths[:, None]
         bias = torch.zeros(B, nk, device=device).masked_fill(
             ~valid, float('-inf')).to(td)[:, None, None, :]
+    elif config == 5:
+        qkv = randn(B, nq, 3, H, D) / math.sqrt(D)
+        q, k, v = qkv.to(td).permute(2, 0, 3, 1, 4)
+        sigma = torch.exp(0.7 + 0.3 * randn(1, H, 1, 1))
+        scale = 1.0 / (2.0 * sigma * sigma)
+        bias = torch.zeros(B, 1, 1, nk, device=device, dtype=td)
+        return Workload(config, dtype, q, k, v, scale, bias, None)
     else:
         raise ValueError(f'unknown config {config}')
     return Workload(config, dtype, q.to(td), k.to(td), v.to(td), scale,
