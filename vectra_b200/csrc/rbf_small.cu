@@ -39,9 +39,11 @@
 namespace vectra {
 namespace {
 
-// Stages of the ring (each one item: Q block, K and V of a plane).
+// Stages of the ring (each one item: Q block, K and V of a plane). Two
+// measured best on the config-5 site (51.4 us; 3 stages 52.0 us, 4 stages
+// 61.4 us): fewer bytes per CTA leave room for more CTAs per SM.
 #ifndef VECTRA_SMALL_STAGES
-#define VECTRA_SMALL_STAGES 3
+#define VECTRA_SMALL_STAGES 2
 #endif
 constexpr int kStages = VECTRA_SMALL_STAGES;
 
