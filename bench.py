@@ -347,8 +347,13 @@ def run_vectra(args):
     for i in range(max(3, args.warmup)):
         step(i)
     if args.profile:
+        # One NVTX range per operator call, named as the reference's
+        # benchmarks name theirs (kernels/benchmarks/bandwidth.py:74-77),
+        # so ncu --nvtx --nvtx-include vectra_region/ selects the same work.
         for i in range(args.steps):
+            torch.cuda.nvtx.range_push('vectra_region')
             step(i)
+            torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         if distributed:
             dist.destroy_process_group()

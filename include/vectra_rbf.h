@@ -133,6 +133,15 @@ VECTRA_API const char* vectra_rbf_strerror(int status);
  * Returns VECTRA_OK, VECTRA_ERR_DEVICE or VECTRA_ERR_CUDA. */
 VECTRA_API int vectra_rbf_check_device_errors(void* stream);
 
+/* Test hook for the failure path (no counterpart in the reference): launches,
+ * on `stream`, a one-thread kernel whose bounded mbarrier wait can never
+ * complete. After about 2 s the wait gives up, records the timeout in the
+ * device error word and the kernel returns, as every kernel of the library
+ * does when a wait runs out; vectra_rbf_check_device_errors then reports
+ * VECTRA_ERR_DEVICE once and the context stays usable. Returns VECTRA_OK or
+ * VECTRA_ERR_CUDA (launch failed). */
+VECTRA_API int vectra_rbf_selftest_wait_timeout(void* stream);
+
 /* Kernels launched by this library in this process (all devices). Tests
  * and the benchmark use it to prove the CUDA path ran. */
 VECTRA_API uint64_t vectra_rbf_launch_count(void);

@@ -5,8 +5,9 @@ collective on the data path (planes are independent,
 kernels/vectra_kernels/spatial_rbf_attention.py:237); these tests check the
 host logic around it with the float64 oracle standing in for the kernel:
 shards partition the batch, broadcast arguments are shared, gathering the
-shards in rank order reproduces the whole-batch result bit for bit, and the
-timing reduction takes the slowest rank.
+shards in rank order reproduces the whole-batch result bit for bit, the
+timing reduction takes the slowest rank, and a rank that fails is reported
+instead of leaving the others waiting.
 """
 
 import os
@@ -98,6 +99,28 @@ def _worker(rank, world, port, n_total):
 def test_two_ranks_reproduce_the_whole_batch(n_total):
     mp.start_processes(_worker, args=(2, _free_port(), n_total), nprocs=2,
                        join=True, start_method='spawn')
+
+
+def _dying_worker(rank, world, port):
+    import datetime  # pylint: disable=import-outside-toplevel
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    try:
+        if rank == 1:
+            raise RuntimeError('rank 1 fails before the gather')
+        sharding.gather_rows(torch.zeros(2, 3), 4)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a_rank_that_dies_is_reported_not_waited_for():
+    # A rank that fails between steps: the launcher reports its error and
+    # ends the rank left waiting in the collective (no hang).
+    with pytest.raises(mp.ProcessRaisedException, match='rank 1 fails'):
+        mp.start_processes(_dying_worker, args=(2, _free_port()), nprocs=2,
+                           join=True, start_method='spawn')
 
 
 def test_reference_arm_runs_on_rank_zero_only(monkeypatch, capsys):

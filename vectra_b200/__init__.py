@@ -3,7 +3,7 @@
 Importing the package registers torch.ops.vectra.rbf_attention with its
 CUDA implementation (hand-written kernels in libvectra_rbf.so behind the C
 ABI of include/vectra_rbf.h). It raises ImportError if the libraries have
-not been built (`python -m vectra_b200.build`).
+not been built (`python vectra_b200/build.py`).
 """
 
 from vectra_b200 import _lib

@@ -34,6 +34,7 @@ EXPORTED = (
     'vectra_rbf_kernel_name',
     'vectra_rbf_strerror',
     'vectra_rbf_check_device_errors',
+    'vectra_rbf_selftest_wait_timeout',
     'vectra_rbf_launch_count',
     'vectra_rbf_build_info',
 )
@@ -57,8 +58,8 @@ class Args(ctypes.Structure):
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f'{LIB_PATH} is missing: build it with `python -m '
-            'vectra_b200.build` (nvcc, sm_100a). vectra_b200 has no CPU or '
+            f'{LIB_PATH} is missing: build it with `python '
+            'vectra_b200/build.py` (nvcc, sm_100a). vectra_b200 has no CPU or '
             'Triton fallback.')
     lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
     lib.vectra_rbf_attention_forward.argtypes = [ctypes.POINTER(Args),
@@ -72,6 +73,8 @@ def _load():
     lib.vectra_rbf_strerror.restype = ctypes.c_char_p
     lib.vectra_rbf_check_device_errors.argtypes = [ctypes.c_void_p]
     lib.vectra_rbf_check_device_errors.restype = ctypes.c_int
+    lib.vectra_rbf_selftest_wait_timeout.argtypes = [ctypes.c_void_p]
+    lib.vectra_rbf_selftest_wait_timeout.restype = ctypes.c_int
     lib.vectra_rbf_launch_count.argtypes = []
     lib.vectra_rbf_launch_count.restype = ctypes.c_uint64
     lib.vectra_rbf_build_info.argtypes = []
@@ -102,4 +105,11 @@ def build_info() -> str:
 def check_device_errors(stream_handle: int = 0) -> int:
     """Synchronises the stream and reads/clears the device error word."""
     return int(LIB.vectra_rbf_check_device_errors(
+        ctypes.c_void_p(stream_handle)))
+
+
+def selftest_wait_timeout(stream_handle: int = 0) -> int:
+    """Launches the failure-path self-test kernel (a bounded wait that runs
+    out after about 2 s); see vectra_rbf_selftest_wait_timeout."""
+    return int(LIB.vectra_rbf_selftest_wait_timeout(
         ctypes.c_void_p(stream_handle)))

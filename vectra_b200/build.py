@@ -5,7 +5,10 @@
 * _vectra_rbf_torch.so: the PyTorch binding that registers the CUDA kernel
   of vectra::rbf_attention; links libvectra_rbf.so through $ORIGIN.
 
-    python -m vectra_b200.build [--force] [--verbose]
+    python vectra_b200/build.py [--force] [--verbose]
+
+(run as a script: `python -m vectra_b200.build` would first import the
+package, which loads the library being rebuilt and fails if it is stale).
 
 Objects go to vectra_b200/_build/ and are rebuilt when a source or header is
 newer. nvcc cross-compiles without a GPU, so this runs on any host with the

@@ -21,6 +21,18 @@ namespace {
 
 std::atomic<uint64_t> g_launches{0};
 
+// Self-test of the kernels' failure path: waits on an mbarrier that nothing
+// ever completes, through the same bounded wait the kernels use
+// (mbar_wait_sleep, about 2 s), which records kErrWaitTimeout in the device
+// error word and returns false. One thread, nothing else to wait for.
+__global__ void wait_timeout_selftest_kernel(unsigned int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(smem_addr(&bar), 1);
+  fence_barrier_init();
+  mbar_wait_sleep(smem_addr(&bar), 0, err);  // no arrive: runs out
+}
+
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm_count[kMaxDevices];
 std::atomic<unsigned int*> g_err_ptr[kMaxDevices];
@@ -284,6 +296,14 @@ int vectra_rbf_check_device_errors(void* stream) {
       cudaSuccess)
     return VECTRA_ERR_CUDA;
   return VECTRA_ERR_DEVICE;
+}
+
+int vectra_rbf_selftest_wait_timeout(void* stream) {
+  unsigned int* err = device_error_ptr();
+  if (err == nullptr) return VECTRA_ERR_CUDA;
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      err);
+  return cudaGetLastError() == cudaSuccess ? VECTRA_OK : VECTRA_ERR_CUDA;
 }
 
 uint64_t vectra_rbf_launch_count(void) {
