@@ -142,54 +142,65 @@ def cpu_model():
     return 'unknown'
 
 
+class CpuRunner:
+    """The oracle's port of the operator's CPU implementation (formulation
+    'matmul', reference.matmul_rbf_attention, the default impl of
+    vectra::rbf_attention) or of the eager chain ('eager',
+    reference.eager_rbf_attention, north_star's CPU path) on `threads` host
+    threads over a fixed sample of the workload, prepared once; run(seconds)
+    times whole passes over it for about `seconds` (at least one pass)."""
+
+    def __init__(self, config, threads, formulation='matmul'):
+        sys.path.insert(0, ROOT)
+        from oracle import rbf_oracle  # pylint: disable=import-outside-toplevel
+        self.config = config
+        fn = (rbf_oracle.eager_rbf_attention if formulation == 'eager'
+              else rbf_oracle.matmul_rbf_attention)
+        what = ('eager-chain port' if formulation == 'eager'
+                else 'matmul port (the op CPU impl)')
+        if config == 4:
+            # One (b, h) plane slice: 64 query rows against all 4096 keys.
+            _, (q, k, v, sc, _b) = cpu_sample(4, 1)
+            q, k, v, sc = q[:, :1, :64], k[:, :1], v[:, :1], sc[:, :1]
+            self.work_items = [None]
+            self.pool = None
+            self.per_pass = 2 * 64 * 4096 * (128 + 128) / 1e12
+            self.unit, self.cores = 'TFLOP/s', 1
+            self.sample = f'{what}, 1 plane x 64 queries x 4096 keys'
+            self._pass = lambda: fn(q, k, v, sc)
+            return
+        n = {1: 8, 5: 32}.get(config, 256)
+        _, (q, k, v, sc, b) = cpu_sample(config, n)
+        chunks = [c for c in np.array_split(np.arange(n), threads) if len(c)]
+        parts = [rbf_oracle.sample_planes(q, k, v, sc, b, c) for c in chunks]
+        self.pool = concurrent.futures.ThreadPoolExecutor(len(parts))
+        self.per_pass = n
+        self.unit, self.cores = metric_for(config)[1], len(parts)
+        self.sample = f'{what}, {n} batch rows per pass'
+        self._pass = lambda: list(self.pool.map(lambda a: fn(*a), parts))
+
+    def run(self, seconds):
+        t0 = time.perf_counter()
+        n = 0
+        while n == 0 or time.perf_counter() - t0 < seconds:
+            self._pass()
+            n += 1
+        return n * self.per_pass / (time.perf_counter() - t0)
+
+    def close(self):
+        if self.pool is not None:
+            self.pool.shutdown()
+
+
 def time_cpu(config, seconds, threads, formulation='matmul'):
-    """Queries/s (or TFLOP/s) of the oracle's port of the operator's CPU
-    implementation (formulation 'matmul', reference.matmul_rbf_attention,
-    the default impl of vectra::rbf_attention) or of the eager chain
-    ('eager', reference.eager_rbf_attention, north_star's CPU path) on
-    `threads` host threads, over a bounded sample for about `seconds`."""
-    sys.path.insert(0, ROOT)
-    from oracle import rbf_oracle  # pylint: disable=import-outside-toplevel
-    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
-    if config == 4:
-        # One (b, h) plane slice: 256 query rows against all 4096 keys.
-        w, (q, k, v, s, b) = cpu_sample(4, 1)
-        q, k, v = q[:, :1, :256], k[:, :1], v[:, :1]
-        s = s[:, :1]
-        flops = 2 * 256 * 4096 * (128 + 128)
-        t0 = time.perf_counter()
-        n = 0
-        while time.perf_counter() - t0 < seconds:
-            rbf_oracle.matmul_rbf_attention(q, k, v, s)
-            n += 1
-        dt = time.perf_counter() - t0
-        return (n * flops / dt / 1e12, 'TFLOP/s', 1,
-                'matmul port, 1 plane x 256 queries x 4096 keys')
-    sample = {1: 8, 5: 32}.get(config, 256)
-    w, (q, k, v, s, b) = cpu_sample(config, sample)
-    chunks = np.array_split(np.arange(q.shape[0]), threads)
-    chunks = [c for c in chunks if len(c)]
-
-    fn = (rbf_oracle.eager_rbf_attention if formulation == 'eager'
-          else rbf_oracle.matmul_rbf_attention)
-
-    def work(idx):
-        sq, sk, sv, ss, sb = rbf_oracle.sample_planes(q, k, v, s, b, idx)
-        fn(sq, sk, sv, ss, sb)
-
-    with concurrent.futures.ThreadPoolExecutor(len(chunks)) as pool:
-        list(pool.map(work, chunks))  # warm-up
-        t0 = time.perf_counter()
-        n = 0
-        while time.perf_counter() - t0 < seconds:
-            list(pool.map(work, chunks))
-            n += 1
-        dt = time.perf_counter() - t0
-    del workloads
-    what = ('eager-chain port' if formulation == 'eager'
-            else 'matmul port (the op CPU impl)')
-    return (n * q.shape[0] / dt, metric_for(config)[1], len(chunks),
-            f'{what}, {q.shape[0]} batch rows x {n} repeats')
+    """One timing of CpuRunner: (value, unit, cores, sample)."""
+    runner = CpuRunner(config, threads, formulation)
+    try:
+        runner.run(min(seconds, 1.0) / 4)  # warm-up
+        value = runner.run(seconds)
+    finally:
+        runner.close()
+    return value, runner.unit, runner.cores, runner.sample
 
 
 def run_reference(args):
@@ -200,13 +211,17 @@ def run_reference(args):
     from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
     metric, unit = metric_for(args.config)
     threads = os.cpu_count() or 1
-    per_step = max(0.2, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
-    for _ in range(args.warmup):
-        time_cpu(args.config, per_step / 4, threads)
-    vals = []
-    for _ in range(args.steps):
-        v, u, cores, sample = time_cpu(args.config, per_step, threads)
-        vals.append(v)
+    # About two minutes in all, whatever K and W are (at least 20 ms of
+    # CPU work per step).
+    per_step = max(0.02, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
+    runner = CpuRunner(args.config, threads)
+    try:
+        for _ in range(args.warmup):
+            runner.run(per_step / 4)
+        vals = [runner.run(per_step) for _ in range(args.steps)]
+    finally:
+        runner.close()
+    cores, sample = runner.cores, runner.sample
     value = float(statistics.median(vals))
     line = {
         'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
