@@ -116,11 +116,16 @@ def _dying_worker(rank, world, port):
 
 
 def test_a_rank_that_dies_is_reported_not_waited_for():
-    # A rank that fails between steps: the launcher reports its error and
-    # ends the rank left waiting in the collective (no hang).
-    with pytest.raises(mp.ProcessRaisedException, match='rank 1 fails'):
+    # A rank that fails between steps: the launcher reports an error (the
+    # failed rank's own, or the surviving rank's broken collective, which
+    # ever arrives first) well before the process group's 20 s timeout.
+    import time  # pylint: disable=import-outside-toplevel
+    t0 = time.monotonic()
+    with pytest.raises(mp.ProcessRaisedException,
+                       match='rank 1 fails|Connection reset|Read error'):
         mp.start_processes(_dying_worker, args=(2, _free_port()), nprocs=2,
                            join=True, start_method='spawn')
+    assert time.monotonic() - t0 < 18
 
 
 def test_reference_arm_runs_on_rank_zero_only(monkeypatch, capsys):
