@@ -1,0 +1,53 @@
+"""The benchmark's contract, on the CPU: the reference arm's one JSON line,
+the metric names per config, and the traffic figures read from the ncu
+summaries in profiles/ (the GPU arm runs on a B200 only)."""
+
+import json
+import os
+
+import pytest
+
+import bench
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_defaults_are_the_headline_config_on_one_gpu():
+    a = bench.parse_args([])
+    assert (a.gpus, a.config, a.impl, a.scaling) == (1, 2, 'vectra', 'weak')
+    assert a.warmup >= 3
+
+
+def test_reference_arm_prints_one_json_line(capfd, monkeypatch):
+    monkeypatch.delenv('RANK', raising=False)
+    assert bench.main(['--impl', 'reference', '--config', '1', '--steps',
+                       '2', '--warmup', '1']) == 0
+    out = capfd.readouterr().out.strip().splitlines()
+    assert len(out) == 1, out
+    line = json.loads(out[0])
+    assert line['impl'] == 'reference'
+    metric, unit = bench.metric_for(1)
+    assert (line['metric'], line['unit']) == (metric, unit)
+    assert line['value'] > 0 and line['higher_is_better'] is True
+    cpu = line['cpu_baseline']
+    assert cpu['value'] == line['value'] and cpu['cores'] >= 1
+    assert cpu['kind'] == 'port' and cpu['cpu_model']
+    assert line['e2e'] == {'value': line['value'], 'unit': unit,
+                           'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}
+
+
+@pytest.mark.parametrize('config', [1, 2, 3, 4, 5])
+def test_metric_units(config):
+    metric, unit = bench.metric_for(config)
+    assert metric and unit == {4: 'TFLOP/s', 5: 'targets/s'}.get(
+        config, 'queries/s')
+
+
+@pytest.mark.parametrize('config,kernel', [(2, 'rbf_decode'),
+                                           (3, 'rbf_decode'),
+                                           (4, 'rbf_tc'), (5, 'rbf_small')])
+def test_traffic_figures_come_from_the_committed_profiles(config, kernel):
+    assert os.path.exists(
+        os.path.join(ROOT, 'profiles', f'{kernel}_config{config}.txt'))
+    traffic = bench.ncu_traffic(config)
+    assert traffic is not None and traffic > 1e8
