@@ -4,7 +4,7 @@
                     [--impl vectra|reference]
 
 One step is one pass of the operator over one batch of the workload
-(default: BASELINE config 2, the serving shape B=1024, H=8, Lq=1, Lk=64,
+(default: benchmark config 2, the serving shape B=1024, H=8, Lq=1, Lk=64,
 D=64, bf16). With N GPUs (torchrun, one process per GPU) every rank
 processes its own batch of the same size (weak scaling; queries are
 independent, there is no collective on the data path) and the value is the
@@ -228,7 +228,7 @@ def run_reference(args):
         'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
         'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
-        'dtype': 'f32', 'data': 'synthetic (seeded, BASELINE config shapes)',
+        'dtype': 'f32', 'data': 'synthetic (seeded, benchmark config shapes)',
         'config': {'workload': workloads.NAMES[args.config],
                    'device': 'host CPU', 'threads': cores},
         'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
@@ -531,7 +531,7 @@ def run_vectra(args):
             'ms_per_step': ms_per_step, 'higher_is_better': True,
             'scaling': args.scaling, 'vs_baseline': None,
             'dtype': w0.dtype,
-            'data': 'synthetic (seeded; BASELINE config shapes and '
+            'data': 'synthetic (seeded; benchmark config shapes and '
                     'distributions)',
             'config': {
                 'workload': workloads.NAMES[args.config],

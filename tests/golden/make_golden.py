@@ -41,7 +41,7 @@ def _cases(torch):
     """Yields (name, dtype, q, k, v, scale, bias, seed-description)."""
     td = {k: getattr(torch, v) for k, v in DTYPES.items()}
 
-    # BASELINE config 1: B=8, H=4, Lq=1, Lk=16, D=32, fp32, N(0,1),
+    # benchmark config 1: B=8, H=4, Lq=1, Lk=16, D=32, fp32, N(0,1),
     # gamma ~ U(0.05, 0.5) per head, no mask.
     gen = torch.Generator().manual_seed(0)
     q = torch.randn(8, 4, 1, 32, generator=gen)
@@ -141,7 +141,7 @@ def _cases(torch):
     yield ('strided_per_head_bias', 'f32', q.contiguous(), k.contiguous(),
            v.contiguous(), torch.full((1, 4, 1, 1), 0.02), bias)
 
-    # BASELINE config 2 (serving), batch cut to 4: bf16, N(0,1)/sqrt(64),
+    # benchmark config 2 (serving), batch cut to 4: bf16, N(0,1)/sqrt(64),
     # gamma ~ U(0.1, 1.0), no mask.
     gen = torch.Generator().manual_seed(2)
     q = torch.randn(4, 8, 1, 64, generator=gen) / 8.0
@@ -151,7 +151,7 @@ def _cases(torch):
     yield ('config2_b4', 'bf16', q.bfloat16(), k.bfloat16(), v.bfloat16(),
            scale, None)
 
-    # BASELINE config 3 (variable comparables), batch cut to 3: clustered
+    # benchmark config 3 (variable comparables), batch cut to 3: clustered
     # keys, prefix mask of length U{8..128} as a 0/-inf bf16 bias.
     gen = torch.Generator().manual_seed(3)
     q = torch.randn(3, 8, 1, 64, generator=gen)

@@ -6,7 +6,7 @@ Tolerances (all written here, used by every parity test):
 * Reference test matrix against the float64 oracle
   (kernels/tests/test_parity.py:33-37): rtol / atol x max|V| of
   fp32 (1e-4, 1e-5), fp16 (1e-3, 1e-3), bf16 (1e-2, 8e-3).
-* BASELINE gate against the eager fp32 formulation: fp32 I/O rtol 1e-3,
+* Acceptance gate against the eager fp32 formulation: fp32 I/O rtol 1e-3,
   atol 1e-5; bf16 (and fp16) I/O rtol 2e-2 with the reference's half
   precision atol 8e-3 x max|V| (a relative bound alone is meaningless for
   outputs near zero).
@@ -22,7 +22,7 @@ TORCH_DTYPES = {'f32': torch.float32, 'f16': torch.float16,
 
 REFERENCE_TOL = {'f32': (1e-4, 1e-5), 'f16': (1e-3, 1e-3),
                  'bf16': (1e-2, 8e-3)}
-BASELINE_TOL = {'f32': (1e-3, 1e-5), 'f16': (2e-2, 8e-3),
+EAGER_GATE_TOL = {'f32': (1e-3, 1e-5), 'f16': (2e-2, 8e-3),
                 'bf16': (2e-2, 8e-3)}
 
 
@@ -60,10 +60,10 @@ def check_reference_tol(actual, q, k, v, scale, bias, dtype):
     assert_close(actual, expected, rtol, atol * float(np.abs(v).max()))
 
 
-def check_baseline_tol(actual, q, k, v, scale, bias, dtype):
-    """BASELINE's gate: the eager fp32 formulation."""
+def check_eager_gate_tol(actual, q, k, v, scale, bias, dtype):
+    """The acceptance gate: the eager fp32 formulation."""
     expected = rbf_oracle.eager_rbf_attention(q, k, v, scale, bias)
-    rtol, atol = BASELINE_TOL[dtype]
+    rtol, atol = EAGER_GATE_TOL[dtype]
     if dtype != 'f32':
         atol *= float(np.abs(v).max())
     assert_close(actual, expected, rtol, atol)

@@ -1,5 +1,5 @@
 """A small price-model-style network whose attention is written as the
-eager RBF chain, for the compiled-model check.
+eager RBF chain, for the compiled-model check (benchmark config 5).
 
 Each block is pre-norm: RBF attention of every token (the target and its
 comparables) over all tokens, with a per-head width sigma_h (coefficient

@@ -1,8 +1,8 @@
-"""BASELINE configs 1-4 and the config-5 attention site at their full sizes
+"""benchmark configs 1-4 and the config-5 attention site at their full sizes
 (B200 only).
 
 The oracle cannot finish a full batch quickly, so each config is checked
-on seeded batch rows against the eager fp32 oracle (BASELINE's gate), and
+on seeded batch rows against the eager fp32 oracle (the acceptance gate), and
 on the whole output through size-independent properties:
 * every output row is a convex combination of the unmasked value rows, so
   each coordinate lies within their per-coordinate min and max;
@@ -58,7 +58,7 @@ def test_serving_configs_full_size(config):
     rows = np.unique(np.linspace(0, B - 1, 24).astype(int))
     q, k, v, s, b = _oracle_rows(inp, rows, inp.dtype)
     got = out[torch.as_tensor(rows).cuda()].double().cpu().numpy()
-    helpers.check_baseline_tol(got, q, k, v, s, b, inp.dtype)
+    helpers.check_eager_gate_tol(got, q, k, v, s, b, inp.dtype)
     helpers.check_reference_tol(got, q, k, v, s, b, inp.dtype)
     half = B // 2
     part = vectra_b200.rbf_attention(
@@ -79,5 +79,5 @@ def test_config4_long_sequence_planes():
     s = inp.scale.float().cpu().numpy()
     want = rbf_oracle.eager_rbf_attention(q, k, v, s)
     got = out[:, :, rows].double().cpu().numpy()
-    rtol, atol = helpers.BASELINE_TOL['bf16']
+    rtol, atol = helpers.EAGER_GATE_TOL['bf16']
     helpers.assert_close(got, want, rtol, atol * float(np.abs(v).max()))

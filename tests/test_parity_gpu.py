@@ -80,7 +80,7 @@ def test_matches_float64_oracle(shape, dtype, with_bias):
     for kernel in _kernels_for(q.shape, shape[4], shape[5], dtype, shape[3]):
         out = helpers.run(q, k, v, scale, bias, dtype, kernel=kernel)
         helpers.check_reference_tol(out, q, k, v, scale, bias, dtype)
-        helpers.check_baseline_tol(out, q, k, v, scale, bias, dtype)
+        helpers.check_eager_gate_tol(out, q, k, v, scale, bias, dtype)
 
 
 def test_output_dtype_shape_and_device():

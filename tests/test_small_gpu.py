@@ -4,7 +4,7 @@
 Key counts on both sides of every tile size it instantiates (32, 64, 80,
 128) and query counts across one and several query blocks; the compiled
 model's layout (q/k/v strided views of one [B, N, 3, H, D] projection,
-BASELINE config 5) with padding masks, fully masked rows (NaN) and per-head
+benchmark config 5) with padding masks, fully masked rows (NaN) and per-head
 biases; degenerate scales; agreement with the generic kernel; determinism
 and batch-slice consistency. Tolerances are the reference suite's
 (kernels/tests/test_parity.py:33-37) and north_star's eager gate.
@@ -45,7 +45,7 @@ def _check(q, k, v, scale, bias, dtype):
     qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
     bn = None if bias is None else bias.float().cpu().numpy()
     helpers.check_reference_tol(got, qn, kn, vn, scale.numpy(), bn, dtype)
-    helpers.check_baseline_tol(got, qn, kn, vn, scale.numpy(), bn, dtype)
+    helpers.check_eager_gate_tol(got, qn, kn, vn, scale.numpy(), bn, dtype)
     return out
 
 

@@ -1,5 +1,5 @@
 // rbf_decode.cu: RBF attention for one query per plane (Nq == 1), the
-// serving shape (a property scored against its Lk
+// serving shape (benchmark configs 1-3: a property scored against its Lk
 // comparables). HBM-bound: every byte of K and V is read exactly once.
 //
 // Design (B200):

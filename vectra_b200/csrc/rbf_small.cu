@@ -1,6 +1,6 @@
 // rbf_small.cu: RBF attention for planes whose keys fit one tile
 // (1 <= Nk <= 128), any Nq >= 2, bf16/f16, D == Dv in {32, 64}. This is the
-// compiled price model's attention site (per site
+// compiled price model's attention site (benchmark config 5: per site
 // B=1024, H=8, Nq=Nk=65, D=32, q/k/v strided views of one projection,
 // models/price_transformer/spatial_attention.py:68-88).
 //

@@ -1,5 +1,5 @@
 // rbf_tc.cu: RBF attention on the 5th-generation tensor cores (tcgen05 +
-// TMEM) for long sequences (B=16, H=16, Lq=Lk=4096,
+// TMEM) for long sequences (benchmark config 4: B=16, H=16, Lq=Lk=4096,
 // D=128, bf16), a true dense contraction.
 //
 // Algebra: the row-constant -g*||q||^2 cancels in the softmax, so

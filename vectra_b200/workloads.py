@@ -1,9 +1,9 @@
-"""Seeded synthetic inputs for the BASELINE configurations, and their
+"""Seeded synthetic inputs for the benchmark configurations, and their
 algorithmic byte / FLOP counts (the roofline numerators).
 
 The reference measures on generated data too (kernels/benchmarks/
-throughput.py:97-111 `problem`); these generators follow BASELINE.json's
-config descriptions instead, with fixed seeds:
+throughput.py:97-111 `problem`); these generators follow the benchmark
+configuration descriptions instead, with fixed seeds:
 
 1. CPU-scale serving: B=8, H=4, Lq=1, Lk=16, D=32, fp32; q,k,v ~ N(0,1);
    gamma_h ~ U(0.05, 0.5); no mask.
@@ -16,13 +16,13 @@ config descriptions instead, with fixed seeds:
    v ~ N(0,1)/sqrt(D); gamma_h ~ U(0.1, 2.0).
 4. Long sequences: B=16, H=16, Lq=Lk=4096, D=128, bf16;
    q,k,v ~ N(0,1)/sqrt(D); gamma_h ~ U(0.01, 0.2); no mask.
-5. One attention site of the compiled price model (
+5. One attention site of the compiled price model (benchmark config 5:
    batch 1024 targets, 64 comparables, d_model 256, 8 heads of D=32, bf16):
    q, k, v are head-transposed views of one [B, N=65, 3, H, D] projection
    (row stride 3*H*D, the layout the compile pass hands the operator),
    projection values ~ N(0,1)/sqrt(D); the coefficient 1/(2 sigma_h^2) with
    log sigma_h ~ N(0.7, 0.3); a [B,1,1,N] bf16 key bias of zeros (every
-   comparable valid, as BASELINE states).
+   comparable valid).
 """
 
 import dataclasses
