@@ -74,14 +74,24 @@ def parse_args(argv=None):
     p.add_argument('--profile', action='store_true',
                    help='warm-up and K steps only (for ncu): no clock soak, '
                         'no e2e, no CPU baseline, no JSON line')
-    return p.parse_args(argv)
+    p.add_argument('--model', action='store_true',
+                   help='config 5 only: the whole compiled model served from '
+                        'CUDA graphs (predictions/s) instead of one site')
+    args = p.parse_args(argv)
+    if args.model and args.config != 5:
+        p.error('--model needs --config 5')
+    return args
 
 
 # ---------------------------------------------------------------------------
 # Shared descriptions
 # ---------------------------------------------------------------------------
 
-def metric_for(config):
+def metric_for(config, model=False):
+    if model:
+        return ('price-model predictions/s, compiled forward with 3 RBF '
+                'sites rewritten (B=1024 targets x 65 tokens, d_model 256, '
+                'H=8 D=32, bf16), CUDA-graph serving', 'predictions/s')
     if config == 5:
         return ('RBF-attn compiled-model site targets/s (B=1024 N=65 H=8 '
                 'D=32 bf16, strided q/k/v)', 'targets/s')
@@ -560,6 +570,266 @@ def run_vectra(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Config 5 at the model level (--model)
+# ---------------------------------------------------------------------------
+
+MODEL_BATCH = 1024      # targets per served batch (benchmark config 5)
+MODEL_LAYERS = 3        # RBF-attention sites
+MODEL_E2E_CHUNKS = 8    # served batches per end-to-end request
+
+
+def load_compile_pass():
+    """The reference's compile pass, installed unmodified in baseline/_ref,
+    with the module name its replacement imports to register the operator
+    (compiler/vectra_compiler/replacement.py:38-39) bound to this library's
+    custom_ops (the one-file swap of kernels/vectra_kernels/custom_ops.py).
+    """
+    import types  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import custom_ops  # pylint: disable=import-outside-toplevel
+    ref = os.path.join(ROOT, 'baseline', '_ref')
+    if not os.path.isdir(os.path.join(ref, 'vectra_compiler')):
+        raise SystemExit('--model needs the reference compile pass in '
+                         'baseline/_ref')
+    pkg = types.ModuleType('vectra_kernels')
+    pkg.__path__ = []
+    pkg.custom_ops = custom_ops
+    sys.modules['vectra_kernels'] = pkg
+    sys.modules['vectra_kernels.custom_ops'] = custom_ops
+    sys.path.insert(0, ref)
+    from vectra_compiler import backend  # pylint: disable=import-outside-toplevel
+    return backend
+
+
+def time_cpu_model(seconds, threads, batch=64):
+    """The model's eager forward on the host CPU (float32, the eager RBF
+    chain at every site, `threads` intra-op threads) over a fixed sample
+    of `batch` targets: (predictions/s, cores, sample)."""
+    import torch  # pylint: disable=import-outside-toplevel
+    from tests import spatial_model  # pylint: disable=import-outside-toplevel
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = spatial_model.SpatialNet(layers=MODEL_LAYERS).eval()
+    args = spatial_model.inputs(batch, seed=1)
+    with torch.no_grad():
+        model(*args)  # warm-up
+        t0 = time.perf_counter()
+        n = 0
+        while n == 0 or time.perf_counter() - t0 < seconds:
+            model(*args)
+            n += 1
+        value = n * batch / (time.perf_counter() - t0)
+    return value, threads, (f'eager float32 model forward, {batch} targets '
+                            f'x 65 tokens per pass, {threads} threads')
+
+
+def run_model_reference(args):
+    """The reference arm at the model level: the eager model on the host's
+    cores (the reference's CPU path for config 5: every site runs the
+    eager RBF chain)."""
+    if int(os.environ.get('RANK', '0')) != 0:
+        return 0
+    sys.path.insert(0, ROOT)
+    metric, unit = metric_for(5, model=True)
+    threads = os.cpu_count() or 1
+    per_step = max(0.05, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        time_cpu_model(per_step / 4, threads)
+    runs = [time_cpu_model(per_step, threads) for _ in range(args.steps)]
+    value = float(statistics.median(r[0] for r in runs))
+    _, cores, sample = runs[0]
+    emit({
+        'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
+        'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'f32', 'data': 'synthetic (seeded, random-init weights)',
+        'config': {'workload': 'config 5 model', 'device': 'host CPU',
+                   'threads': cores},
+        'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
+                         'kind': 'port', 'sample': sample,
+                         'cpu_model': cpu_model()},
+        'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
+                'd2h_bytes_per_step': 0},
+    })
+    return 0
+
+
+def run_model(args):
+    """Config 5 served whole: the compiled model (every RBF site rewritten
+    to this library's operator by the reference's compile pass) captured
+    in CUDA graphs and served through vectra_b200.serving.
+
+    value: predictions/s with the requests resident in HBM, one step = one
+    served batch of 1,024 targets (GraphServingModel.predict: copy into a
+    static batch, replay, float result). e2e: one step = one request of
+    8 x 1,024 targets from pinned host memory through predict, result
+    copied back to the host. The forward's activations (34 MB per tensor
+    per layer) exceed L2, so no flush is needed between steps.
+    """
+    import torch  # pylint: disable=import-outside-toplevel
+    import torch.distributed as dist  # pylint: disable=import-outside-toplevel
+    sys.path.insert(0, ROOT)
+    import vectra_b200  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import serving  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+    from tests import spatial_model  # pylint: disable=import-outside-toplevel
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    distributed = world > 1
+    if distributed:
+        import datetime  # pylint: disable=import-outside-toplevel
+        dist.init_process_group('nccl', device_id=dev,
+                                timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if distributed:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    backend = load_compile_pass()
+    torch.manual_seed(0)
+    model = spatial_model.SpatialNet(layers=MODEL_LAYERS).to(dev).eval()
+    model = model.to(torch.bfloat16)
+    example = spatial_model.inputs(MODEL_BATCH, device=dev,
+                                   dtype=torch.bfloat16, seed=1000 * rank)
+    compiled, report = backend.compile_for_serving(
+        model, example, expected_sites=MODEL_LAYERS)
+    if report.sites != MODEL_LAYERS or report.graph_break_count:
+        raise SystemExit(f'compile pass rewrote {report.sites} sites with '
+                         f'{report.graph_break_count} graph breaks')
+    before = vectra_b200.launch_count()
+    gs = serving.GraphServingModel(compiled, example)
+    per_capture = (vectra_b200.launch_count() - before) // (2 + 2)
+    sets = [spatial_model.inputs(MODEL_BATCH, device=dev,
+                                 dtype=torch.bfloat16, seed=1000 * rank + i)
+            for i in range(1, 5)]
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(3, args.warmup)):
+        gs.predict(sets[i % len(sets)])
+    sampler = ClockSampler(local)
+    torch.cuda.synchronize()
+    t_soak = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_soak < 0.6:
+        gs.predict(sets[i % len(sets)])
+        i += 1
+        if i % 8 == 0:
+            torch.cuda.synchronize()
+
+    # Timed region: exactly K served batches.
+    r0 = torch.cuda.Event(enable_timing=True)
+    r1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    r0.record(stream)
+    for i in range(args.steps):
+        gs.predict(sets[i % len(sets)])
+    r1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    region_ms = r0.elapsed_time(r1)
+    ms_per_step = sharding.max_over_ranks(region_ms, device=dev) / args.steps
+    value = MODEL_BATCH * world / (ms_per_step * 1e-3)
+
+    # End to end: requests of 8 served batches from pinned host memory,
+    # result read back to the host; the chunks of one request pipeline
+    # their host-to-device copies under the previous chunk's forward.
+    n_e2e = MODEL_E2E_CHUNKS * MODEL_BATCH
+    host = [t.pin_memory() for t in spatial_model.inputs(
+        n_e2e, dtype=torch.bfloat16, seed=7 + rank)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    e2e_steps = max(3, min(args.e2e_steps, args.steps))
+    for _ in range(2):
+        gs.predict(host).cpu()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        result = gs.predict(host).cpu()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    d2h = result.numel() * result.element_size()
+    e2e_ms = sharding.max_over_ranks(e0.elapsed_time(e1),
+                                     device=dev) / e2e_steps
+    e2e_value = n_e2e * world / (e2e_ms * 1e-3)
+
+    # The site kernel on its own, on the sites' shapes (benchmark config 5's
+    # site workload), event-timed over back-to-back calls.
+    hbm, _, peak_kind = peaks()
+    site_sets = [workloads.make(5, device=dev, seed=i) for i in range(4)]
+    op = torch.ops.vectra.rbf_attention
+    for w in site_sets:
+        op(*w.tensors())
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    n_site = 200
+    s0.record(stream)
+    for i in range(n_site):
+        op(*site_sets[i % 4].tensors())
+    s1.record(stream)
+    torch.cuda.synchronize()
+    site_ms = s0.elapsed_time(s1) / n_site
+    alg_bytes = workloads.algorithmic_bytes(site_sets[0])
+    achieved = alg_bytes / (site_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = time_cpu_model(args.cpu_seconds,
+                                          os.cpu_count() or 1)
+        cpu = {'value': v, 'unit': 'predictions/s', 'cores': cores,
+               'kind': 'port', 'sample': sample, 'cpu_model': cpu_model()}
+    if rank == 0:
+        metric, unit = metric_for(5, model=True)
+        emit({
+            'metric': metric, 'value': value, 'unit': unit, 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms_per_step, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
+            'data': 'synthetic (seeded inputs, random-init weights)',
+            'config': {
+                'workload': 'config 5 model: compiled 3-block price-model-'
+                            'style network (tests/spatial_model.py), '
+                            f'{MODEL_BATCH} targets x 65 tokens per batch',
+                'global_batch': MODEL_BATCH * world,
+                'parallelism': f'one served batch per GPU x{world}, no '
+                               'collective',
+                'compile': {'sites': report.sites,
+                            'graph_count': report.graph_count,
+                            'graph_break_count': report.graph_break_count},
+                'serving': 'vectra_b200.serving.GraphServingModel, 2 slots',
+                'l2': 'activations 34 MB per tensor per layer (> L2)',
+            },
+            'e2e': {'value': e2e_value, 'unit': unit,
+                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                    'steps': e2e_steps,
+                    'targets_per_step': n_e2e},
+            'gpu_launches': per_capture * args.steps,
+            'roofline': {
+                'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
+                'unit': 'GB/s', 'frac': achieved / hbm,
+                'traffic': ncu_traffic(5),
+                'peak_kind': f'HBM copy, {peak_kind}',
+                'kernel': 'rbf_small, one site, timed alone',
+                'algorithmic_bytes_per_launch': alg_bytes,
+                'site_ms': site_ms,
+                'sites_share_of_forward': MODEL_LAYERS * site_ms /
+                                          ms_per_step},
+            'cpu_baseline': cpu,
+            'clocks': clocks,
+        })
+    del gs
+    if distributed:
+        dist.destroy_process_group()
+    return 0
+
+
 # The JSON line goes to the process's original standard output; while the
 # benchmark runs, file descriptor 1 points at standard error, so that what
 # libraries print there (NCCL's version banner, for one) cannot come before
@@ -582,8 +852,9 @@ def main(argv=None):
         _RESULT_OUT = os.fdopen(os.dup(saved), 'w')
         os.dup2(2, 1)
         if args.impl == 'reference':
-            return run_reference(args)
-        return run_vectra(args)
+            return (run_model_reference(args) if args.model
+                    else run_reference(args))
+        return run_model(args) if args.model else run_vectra(args)
     finally:
         sys.stdout.flush()
         os.dup2(saved, 1)

@@ -51,3 +51,22 @@ def test_traffic_figures_come_from_the_committed_profiles(config, kernel):
         os.path.join(ROOT, 'profiles', f'{kernel}_config{config}.txt'))
     traffic = bench.ncu_traffic(config)
     assert traffic is not None and traffic > 1e8
+
+
+def test_model_mode_needs_config_5():
+    with pytest.raises(SystemExit):
+        bench.parse_args(['--model'])
+    assert bench.parse_args(['--model', '--config', '5']).model
+    assert bench.metric_for(5, model=True)[1] == 'predictions/s'
+
+
+def test_model_reference_arm_prints_one_json_line(capfd, monkeypatch):
+    monkeypatch.delenv('RANK', raising=False)
+    assert bench.main(['--impl', 'reference', '--config', '5', '--model',
+                       '--steps', '1', '--warmup', '0']) == 0
+    out = capfd.readouterr().out.strip().splitlines()
+    assert len(out) == 1, out
+    line = json.loads(out[0])
+    assert line['impl'] == 'reference' and line['unit'] == 'predictions/s'
+    assert line['value'] > 0 and line['cpu_baseline']['cores'] >= 1
+    assert line['e2e']['h2d_bytes_per_step'] == 0

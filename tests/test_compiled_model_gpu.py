@@ -13,48 +13,18 @@ the rewritten sites. The model (tests/spatial_model.py) writes its
 attention as the eager RBF chain, as the price model does.
 """
 
-import os
-import sys
-import types
-
 import pytest
 import torch
 
 from tests import spatial_model
-
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.path.join(ROOT, 'baseline', '_ref')
+from tests.conftest import compile_pass_installed
 
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(
-        not os.path.isdir(os.path.join(REF, 'vectra_compiler')),
+        not compile_pass_installed(),
         reason='the reference compile pass is not installed in baseline/_ref'),
 ]
-
-
-@pytest.fixture(scope='module')
-def backend():
-    import vectra_b200  # pylint: disable=import-outside-toplevel,unused-import
-    from vectra_b200 import custom_ops  # pylint: disable=import-outside-toplevel
-    names = ('vectra_kernels', 'vectra_kernels.custom_ops')
-    saved = {n: sys.modules.get(n) for n in names}
-    pkg = types.ModuleType('vectra_kernels')
-    pkg.__path__ = []
-    pkg.custom_ops = custom_ops
-    sys.modules['vectra_kernels'] = pkg
-    sys.modules['vectra_kernels.custom_ops'] = custom_ops
-    sys.path.insert(0, REF)
-    try:
-        from vectra_compiler import backend as b  # pylint: disable=import-outside-toplevel
-        yield b
-    finally:
-        sys.path.remove(REF)
-        for n, m in saved.items():
-            if m is None:
-                sys.modules.pop(n, None)
-            else:
-                sys.modules[n] = m
 
 
 def _rel(a, b):
