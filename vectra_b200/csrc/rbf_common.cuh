@@ -106,6 +106,38 @@ __device__ __forceinline__ float load_bias(const RbfProblem& p, int64_t b,
                   b * p.sb[0] + h * p.sb[1] + key * p.sb[2]);
 }
 
+// The bits of a bias element, loaded without converting it, so that the
+// load can stay in flight until the value is used: 32-bit elements as they
+// are, 16-bit ones zero-extended; a float64 bias is converted to float32
+// bits on the spot.
+__device__ __forceinline__ uint32_t load_bias_bits(const RbfProblem& p,
+                                                   int64_t b, int64_t h,
+                                                   int64_t key) {
+  const int64_t idx = b * p.sb[0] + h * p.sb[1] + key * p.sb[2];
+  switch (p.bias_dtype) {
+    case VECTRA_F32:
+      return __ldg(static_cast<const unsigned int*>(p.bias) + idx);
+    case VECTRA_F16:
+    case VECTRA_BF16:
+      return __ldg(static_cast<const unsigned short*>(p.bias) + idx);
+    default:
+      return __float_as_uint(
+          static_cast<float>(__ldg(static_cast<const double*>(p.bias) + idx)));
+  }
+}
+
+// The float value of bits from load_bias_bits.
+__device__ __forceinline__ float bias_bits_to_f32(uint32_t w, int dtype) {
+  switch (dtype) {
+    case VECTRA_F16:
+      return __half2float(__ushort_as_half(static_cast<unsigned short>(w)));
+    case VECTRA_BF16:
+      return __uint_as_float(w << 16);
+    default:
+      return __uint_as_float(w);
+  }
+}
+
 // 2^x on the SFU (ex2.approx: relative error ~2^-22; 2^-inf = +0).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -76,6 +76,11 @@ constexpr int kLargeStageWarps = VECTRA_DECODE_LARGE_WARPS;
 #ifndef VECTRA_DECODE_SKIP_EMPTY
 #define VECTRA_DECODE_SKIP_EMPTY 1
 #endif
+// 1: problems with a key bias use the byte-ring kernel below
+// (rbf_decode_masked_kernel); 0: the fixed-stage kernel.
+#ifndef VECTRA_DECODE_MASK_RING
+#define VECTRA_DECODE_MASK_RING 1
+#endif
 // 1: keys and values are copied with an L2 evict-first policy (they are
 // read exactly once); 0: default L2 policy.
 #ifndef VECTRA_DECODE_L2_EVICT_FIRST
@@ -610,11 +615,542 @@ struct DecodeLauncher {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Masked problems (a key bias is given): exact-size items in a byte ring.
+// ---------------------------------------------------------------------------
+// The items are those above, (plane slot g, chunk c), with chunks of up to
+// 128 keys, but an item occupies exactly the shared memory it needs: the q
+// row and the key and value rows lo..hi (its first and last keys with a
+// finite bias), packed from row 0. kMaskProducers producer warps, which make
+// no global loads (their release stores would wait for them), each work
+// through every kMaskProducers-th item in order, in their own quarter of a
+// byte ring: item i uses slot i % kMaskSlots (an mbarrier for its rows, one
+// for its bias row, a staging row for the bias and its ring placement); the
+// bias row of the producer's item kMaskAhead ahead is bulk-copied while item
+// i is issued; from the staged biases the producer finds lo..hi, allocates
+// the item, arms the slot and copies the rows. Consumer warps compute as
+// above and mark items done; each producer frees its ring quarter in item
+// order. With variable key counts (benchmark config 3: 8..128 valid keys per
+// query) the ring then holds as many bytes in flight as the live rows need,
+// instead of fixed stages sized for a full chunk (measured: 139 us against
+// 149 us for the fixed stages; one producer warp alone was the bottleneck at
+// 293-409 us, two at 207 us).
+#ifndef VECTRA_MASK_WARPS
+#define VECTRA_MASK_WARPS 8
+#endif
+constexpr int kMaskSlots = 64;
+#ifndef VECTRA_MASK_PRODUCERS
+#define VECTRA_MASK_PRODUCERS 4
+#endif
+constexpr int kMaskProducers = VECTRA_MASK_PRODUCERS;  // producer warps
+static_assert(kMaskSlots % kMaskProducers == 0, "slots per producer");
+#ifndef VECTRA_MASK_AHEAD
+#define VECTRA_MASK_AHEAD 4
+#endif
+constexpr int kMaskAhead = VECTRA_MASK_AHEAD;  // bias rows fetched ahead
+#ifndef VECTRA_MASK_POLL_NS
+#define VECTRA_MASK_POLL_NS 128
+#endif
+#ifndef VECTRA_MASK_CONSUMER_SLEEP
+#define VECTRA_MASK_CONSUMER_SLEEP 0
+#endif
+constexpr int kMaskItemBytes = 32768;  // key + value bytes of a full chunk
+
+struct MaskLaunch {
+  int n_planes;     // B * H
+  int H;
+  int nchunks;      // ceil(Nk / KC)
+  int k_contig;
+  int v_contig;
+  int bias_es;      // bytes per bias element (2 or 4)
+  int bias_row;     // bytes per staged bias row (KC * bias_es)
+  int ring_bytes;   // multiple of 128
+  int stage_area;   // byte offset of the bias staging rows
+  int warp_area;    // byte offset of the consumers' per-warp areas
+};
+
+// Bounded wait for a shared-memory word published with a release store,
+// with a short back-off (the producer publishes items every few hundred
+// cycles).
+__device__ __forceinline__ bool wait_smem_equals_short(const int* ptr,
+                                                       int want,
+                                                       unsigned int* err) {
+  for (uint32_t i = 0; i < kSleepWaitLimit; ++i) {
+    if (ld_acquire_smem(ptr) == want) return true;
+    __nanosleep(VECTRA_MASK_POLL_NS);
+  }
+  report_error(err, kErrWaitTimeout);
+  return false;
+}
+
+// Bias element j of a staged row, exp2 domain.
+__device__ __forceinline__ float staged_bias(const uint8_t* row, int j,
+                                             int es, int dtype) {
+  const uint32_t w = es == 4 ? reinterpret_cast<const uint32_t*>(row)[j]
+                             : reinterpret_cast<const uint16_t*>(row)[j];
+  return bias_bits_to_f32(w, dtype) * kLog2e;
+}
+
+template <typename T, int D, int DV, int KC, int WARPS>
+__global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
+    rbf_decode_masked_kernel(RbfProblem p, MaskLaunch L) {
+  using Cfg = DecodeCfg<T, D, DV, KC>;
+  constexpr int ES = Cfg::ES, E = Cfg::E, P = Cfg::P, C = Cfg::C;
+  constexpr int CV = Cfg::CV, RV = Cfg::RV, QB = Cfg::QB, KPL = Cfg::KPL;
+  constexpr int NSLOT = kMaskSlots;
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Layout: ring | row mbarriers | bias mbarriers | item meta {offset, lo,
+  // hi, item} | done | bias staging rows | consumers' q32 and
+  // probabilities.
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.ring_bytes);
+  uint64_t* bbars = bars + NSLOT;
+  int4* meta = reinterpret_cast<int4*>(bbars + NSLOT);
+  int* done = reinterpret_cast<int*>(meta + NSLOT);
+  uint8_t* bstage = smem + L.stage_area;
+
+  const T* __restrict__ gq = static_cast<const T*>(p.q);
+  const T* __restrict__ gk = static_cast<const T*>(p.k);
+  const T* __restrict__ gv = static_cast<const T*>(p.v);
+  T* __restrict__ gout = static_cast<T*>(p.out);
+  const uint64_t stream_policy = VECTRA_DECODE_L2_EVICT_FIRST
+                                     ? l2_evict_first_policy()
+                                     : l2_evict_normal_policy();
+  const int nk = static_cast<int>(p.Nk);
+  const int nchunks = L.nchunks;
+  const int n_slots = (L.n_planes - 1 - int(blockIdx.x)) / int(gridDim.x) + 1;
+  const int n_items = n_slots * nchunks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(smem_addr(&bars[s]), 1);
+      mbar_init(smem_addr(&bbars[s]), 1);
+      meta[s] = make_int4(0, 0, -1, -1);
+      done[s] = -1;
+    }
+    fence_barrier_init();
+  }
+  allow_dependents();
+  __syncthreads();
+  // Every global access (inputs, output, error word) comes after this.
+  grid_dependency_wait();
+
+  if (warp >= WARPS) {
+    // ----------------------------------------------------------- producers
+    // Producer pr owns items pr, pr + kMaskProducers, ... and the ring
+    // quarter [pr R / 4, (pr + 1) R / 4); its items' slots (i % kMaskSlots)
+    // are its own too, so the producers never touch each other's state.
+    const int pr = warp - WARPS;
+    const int step = kMaskProducers;
+    const int rbase = (L.ring_bytes / kMaskProducers / 128 * 128) * pr;
+    const int rsize = L.ring_bytes / kMaskProducers / 128 * 128;
+    // Item k is issued by lane k % 32: a lane's proxy fence and release
+    // stores wait for its own earlier copies, which are then 32 items old.
+    // Bulk copy of item i's bias row into its slot's staging row.
+    auto fetch_bias = [&](int i) {
+      const int g = i / nchunks, chunk = i - g * nchunks;
+      const int plane = int(blockIdx.x) + g * int(gridDim.x);
+      const int b = plane / L.H, h = plane - b * L.H;
+      const int kbase = chunk * KC;
+      const uint32_t bytes = uint32_t(min(KC, nk - kbase) * L.bias_es);
+      const int s = i % NSLOT;
+      const uint8_t* src = static_cast<const uint8_t*>(p.bias) +
+                           (b * p.sb[0] + h * p.sb[1] + kbase) * L.bias_es;
+      mbar_arrive_expect_tx(smem_addr(&bbars[s]), bytes);
+      bulk_g2s(smem_addr(bstage + s * L.bias_row), src, bytes,
+               smem_addr(&bbars[s]), stream_policy);
+    };
+    for (int a = 0; a < kMaskAhead; ++a) {
+      const int i = pr + a * step;
+      if (i < n_items && lane == ((i / step) & 31)) fetch_bias(i);
+    }
+    int tail = pr;  // oldest item of this producer not yet freed
+    int head = 0;   // next free byte of this producer's ring quarter
+    bool ok = true;
+    for (int k = pr; k < n_items && ok; k += step) {
+      const int slot = k % NSLOT;
+      // The item's biases (exp2 domain, -inf past the last key) and its
+      // live key range.
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(smem_addr(&bbars[slot]),
+                                uint32_t((k / NSLOT) & 1), p.err));
+      if (!ok) break;
+      const int cnt = min(KC, nk - (k % nchunks) * KC);
+      const uint8_t* brow = bstage + slot * L.bias_row;
+      int lo = KC, hi = -1;
+#pragma unroll
+      for (int t = 0; t < KPL; ++t) {
+        const int j = lane + 32 * t;
+        const float bv =
+            j < cnt ? staged_bias(brow, j, L.bias_es, p.bias_dtype) : kNegInf;
+        const unsigned live = __ballot_sync(0xffffffffu, bv != kNegInf);
+        if (live) {
+          lo = min(lo, 32 * t + __ffs(live) - 1);
+          hi = max(hi, 32 * t + 31 - __clz(live));
+        }
+      }
+      const int nrows = hi >= lo ? hi - lo + 1 : 0;
+      const int sz = (QB + nrows * (D + DV) * ES + 127) & ~127;
+      // Allocate [off, off + sz) after the live region, freeing done items
+      // in order (lane 0 reads the flags; the warp agrees on the result).
+      // The bias slot fetched next (item k + kMaskAhead) must be free too.
+      const int ahead = k + kMaskAhead * step;
+      const int need_free = ahead < n_items ? ahead : k;
+      int off = -1;
+      for (uint32_t it = 0; it < kSleepWaitLimit; ++it) {
+        int t_new = tail, ub = 0;
+        if (lane == 0) {
+          while (t_new < k && ld_acquire_smem(&done[t_new % NSLOT]) == t_new)
+            t_new += step;
+          if (t_new < k) ub = meta[t_new % NSLOT].x - rbase;
+        }
+        t_new = __shfl_sync(0xffffffffu, t_new, 0);
+        ub = __shfl_sync(0xffffffffu, ub, 0);
+        tail = t_new;
+        if (need_free - tail < NSLOT) {  // slots of items tail..need_free
+          if (k == tail) {
+            off = 0;  // nothing live: start over at the beginning
+          } else if (head > ub) {  // live bytes [ub, head)
+            if (head + sz <= rsize)
+              off = head;
+            else if (sz <= ub)
+              off = 0;
+          } else if (head + sz <= ub) {  // live [ub, end) and [0, head)
+            off = head;
+          }
+        }
+        if (off >= 0) break;
+        __nanosleep(64);
+      }
+      if (off < 0) {
+        if (lane == 0) report_error(p.err, kErrWaitTimeout);
+        ok = false;
+        break;
+      }
+      head = off + sz;
+      const int g = k / nchunks, chunk = k - g * nchunks;
+      const int plane = int(blockIdx.x) + g * int(gridDim.x);
+      const int b = plane / L.H, h = plane - b * L.H;
+      const int kbase = chunk * KC;
+      uint8_t* st = ring + rbase + off;
+      const uint32_t bar = smem_addr(&bars[slot]);
+      uint8_t* kd = st + QB;
+      uint8_t* vd = kd + size_t(nrows) * D * ES;
+      const int il = (k / step) & 31;  // this item's issuing lane
+      __syncwarp();
+      if (lane == il) {
+        meta[slot] = make_int4(rbase + off, lo, hi, meta[slot].w);
+        // Consumers' reads of the freed bytes and bias rows (released with
+        // their done flags, acquired above) come before these async writes.
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, QB + nrows * (D + DV) * ES);
+        bulk_g2s(smem_addr(st), gq + b * p.sq[0] + h * p.sq[1], QB, bar,
+                 stream_policy);
+        if (nrows > 0 && L.k_contig)
+          bulk_g2s(smem_addr(kd),
+                   gk + b * p.sk[0] + h * p.sk[1] +
+                       int64_t(kbase + lo) * p.sk[2],
+                   nrows * D * ES, bar, stream_policy);
+        if (nrows > 0 && L.v_contig)
+          bulk_g2s(smem_addr(vd),
+                   gv + b * p.sv[0] + h * p.sv[1] +
+                       int64_t(kbase + lo) * p.sv[2],
+                   nrows * DV * ES, bar, stream_policy);
+      }
+      __syncwarp();  // the slot is armed before any lane's row copies
+      if (nrows > 0 && !L.k_contig) {
+        const T* k0p =
+            gk + b * p.sk[0] + h * p.sk[1] + int64_t(kbase + lo) * p.sk[2];
+        for (int r = lane; r < nrows; r += 32)
+          bulk_g2s(smem_addr(kd + size_t(r) * D * ES), k0p + r * p.sk[2],
+                   D * ES, bar, stream_policy);
+      }
+      if (nrows > 0 && !L.v_contig) {
+        const T* v0p =
+            gv + b * p.sv[0] + h * p.sv[1] + int64_t(kbase + lo) * p.sv[2];
+        for (int r = lane; r < nrows; r += 32)
+          bulk_g2s(smem_addr(vd + size_t(r) * DV * ES), v0p + r * p.sv[2],
+                   DV * ES, bar, stream_policy);
+      }
+      __syncwarp();
+      if (lane == il) {
+        if (ahead < n_items) fetch_bias(ahead);
+        st_release_smem(&meta[slot].w, k);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  float* q32 = reinterpret_cast<float*>(smem + L.warp_area) + warp * (D + KC);
+  float* pvals = q32 + D;
+  const int rot = lane / Cfg::ROT_DIV;
+  const int vrow = lane / CV;        // value row within a warp step
+  const int vchunk = lane - vrow * CV;
+
+  for (int g = warp; g < n_slots; g += WARPS) {
+    const int plane = int(blockIdx.x) + g * int(gridDim.x);
+    const int b = plane / L.H, h = plane - b * L.H;
+    const float g2 = load_scale(p, b, h) * kLog2e;
+    float m = kNegInf, l = 0.f;
+    uint64_t acc[P];
+#pragma unroll
+    for (int e = 0; e < P; ++e) acc[e] = 0;
+
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
+      const int i = g * nchunks + chunk;
+      const int slot = i % NSLOT;
+      if (!wait_smem_equals_short(&meta[slot].w, i, p.err) ||
+          !(VECTRA_MASK_CONSUMER_SLEEP
+                ? mbar_wait_sleep(smem_addr(&bars[slot]),
+                                  uint32_t((i / NSLOT) & 1), p.err)
+                : mbar_wait(smem_addr(&bars[slot]),
+                            uint32_t((i / NSLOT) & 1), p.err)))
+        return;  // error recorded; the host reports it
+      const int4 md = meta[slot];
+      const int lo = md.y, hi = md.z;
+      const int nrows = hi >= lo ? hi - lo + 1 : 0;
+      const uint8_t* st = ring + md.x;
+      const uint8_t* brow = bstage + slot * L.bias_row;
+      const uint8_t* ks = st + QB;
+      const uint8_t* vs = ks + size_t(nrows) * D * ES + vchunk * 16;
+
+      if (chunk == 0) {
+        const T* sq = reinterpret_cast<const T*>(st);
+        for (int d = lane; d < D; d += 32) {
+          const int ch = d / E, e = d - (d / E) * E;
+          q32[((e >> 2) * C + ch) * 4 + (e & 3)] = to_f32(sq[d]);
+        }
+        __syncwarp();
+      }
+
+      if (nrows > 0) {
+      // Squared distances (rows packed from key lo; lanes whose key is
+      // outside lo..hi read row 0 and are masked below).
+      uint64_t dacc[KPL][4];
+#pragma unroll
+      for (int t = 0; t < KPL; ++t)
+        dacc[t][0] = dacc[t][1] = dacc[t][2] = dacc[t][3] = 0;
+#pragma unroll
+      for (int cc = 0; cc < C; ++cc) {
+        const int ch = (cc + rot) & (C - 1);
+        uint64_t qv[P];
+#pragma unroll
+        for (int pp = 0; pp < E / 4; ++pp) {
+          const float4 t4 =
+              *reinterpret_cast<const float4*>(&q32[(pp * C + ch) * 4]);
+          qv[2 * pp] = pk(t4.x, t4.y);
+          qv[2 * pp + 1] = pk(t4.z, t4.w);
+        }
+#pragma unroll
+        for (int t = 0; t < KPL; ++t) {
+          const int j = lane + 32 * t;
+          const int r = (j >= lo && j <= hi) ? j - lo : 0;
+          const uint4 raw = *reinterpret_cast<const uint4*>(
+              ks + size_t(r) * D * ES + ch * 16);
+          uint64_t kv[P];
+          chunk_pairs<T>(raw, kv);
+#pragma unroll
+          for (int e = 0; e < P; ++e) {
+            const uint64_t diff = sub2(qv[e], kv[e]);
+            uint64_t& a = dacc[t][(e + cc * P) & 3];
+            a = fma2(diff, diff, a);
+          }
+        }
+      }
+
+      // Exact softmax of the chunk, merged online into (m, l, acc).
+      float sc[KPL];
+      float cmax = kNegInf;
+#pragma unroll
+      for (int t = 0; t < KPL; ++t) {
+        const int j = lane + 32 * t;
+        const float2 a0 = upk(dacc[t][0]), a1 = upk(dacc[t][1]);
+        const float2 a2 = upk(dacc[t][2]), a3 = upk(dacc[t][3]);
+        const float dist =
+            ((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y));
+        sc[t] = (j >= lo && j <= hi)
+                    ? fmaf(-g2, dist,
+                           staged_bias(brow, j, L.bias_es, p.bias_dtype))
+                    : kNegInf;
+        cmax = fmaxf(cmax, sc[t]);
+      }
+      float lsum = 0.f;
+      {
+        const float lsafe = (cmax == kNegInf) ? 0.f : cmax;
+#pragma unroll
+        for (int t = 0; t < KPL; ++t) lsum += fast_exp2(sc[t] - lsafe);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, cmax, o);
+        const float ol = __shfl_xor_sync(0xffffffffu, lsum, o);
+        const float nm = fmaxf(cmax, om);
+        const float ns_ = (nm == kNegInf) ? 0.f : nm;
+        lsum = lsum * fast_exp2(cmax - ns_) + ol * fast_exp2(om - ns_);
+        cmax = nm;
+      }
+      const float m_new = fmaxf(m, cmax);
+      const float safe = (m_new == kNegInf) ? 0.f : m_new;
+      const float alpha = fast_exp2(m - safe);
+      l = fmaf(l, alpha, lsum * fast_exp2(cmax - safe));
+#pragma unroll
+      for (int t = 0; t < KPL; ++t)
+        pvals[lane + 32 * t] = fast_exp2(sc[t] - safe);
+      m = m_new;
+      __syncwarp();
+
+      // acc = alpha * acc + sum_j p_j v_j over this lane's row group; value
+      // row j - lo holds key j.
+      const uint64_t alpha2 = pk(alpha, alpha);
+#pragma unroll
+      for (int e = 0; e < P; ++e) acc[e] = mul2(acc[e], alpha2);
+      uint64_t acc_b[P];
+#pragma unroll
+      for (int e = 0; e < P; ++e) acc_b[e] = 0;
+      int j = lo + vrow;
+      for (; j + RV <= hi; j += 2 * RV) {
+        const float p0 = pvals[j], p1 = pvals[j + RV];
+        const uint4 r0 = *reinterpret_cast<const uint4*>(
+            vs + size_t(j - lo) * DV * ES);
+        const uint4 r1 = *reinterpret_cast<const uint4*>(
+            vs + size_t(j - lo + RV) * DV * ES);
+        uint64_t v0[P], v1[P];
+        chunk_pairs<T>(r0, v0);
+        chunk_pairs<T>(r1, v1);
+        const uint64_t pp0 = pk(p0, p0), pp1 = pk(p1, p1);
+#pragma unroll
+        for (int e = 0; e < P; ++e) {
+          acc[e] = fma2(pp0, v0[e], acc[e]);
+          acc_b[e] = fma2(pp1, v1[e], acc_b[e]);
+        }
+      }
+      if (j <= hi) {
+        const float p0 = pvals[j];
+        const uint4 r0 = *reinterpret_cast<const uint4*>(
+            vs + size_t(j - lo) * DV * ES);
+        uint64_t v0[P];
+        chunk_pairs<T>(r0, v0);
+        const uint64_t pp0 = pk(p0, p0);
+#pragma unroll
+        for (int e = 0; e < P; ++e) acc[e] = fma2(pp0, v0[e], acc[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < P; ++e) {
+        const float2 a = upk(acc[e]), bb = upk(acc_b[e]);
+        acc[e] = pk(a.x + bb.x, a.y + bb.y);
+      }
+      }
+      __syncwarp();  // every lane is done with the item, its bias and pvals
+      if (lane == 0) st_release_smem(&done[slot], i);
+    }
+
+    // Sum the row groups, normalise, store 16 bytes per lane of group 0.
+    // Fully masked rows: l == 0 and acc == 0, so 0 * inf = NaN as in the
+    // reference.
+    float o[E];
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+      float2 a = upk(acc[e]);
+#pragma unroll
+      for (int off = CV; off < 32; off <<= 1) {
+        a.x += __shfl_xor_sync(0xffffffffu, a.x, off);
+        a.y += __shfl_xor_sync(0xffffffffu, a.y, off);
+      }
+      o[2 * e] = a.x;
+      o[2 * e + 1] = a.y;
+    }
+    if (vrow == 0) {
+      const float inv = 1.f / l;
+      union {
+        T e[E];
+        uint4 u;
+      } pack;
+#pragma unroll
+      for (int e = 0; e < E; ++e) pack.e[e] = from_f32<T>(o[e] * inv);
+      *reinterpret_cast<uint4*>(gout + b * p.so[0] + h * p.so[1] +
+                                vchunk * E) = pack.u;
+    }
+  }
+}
+
+// Whether the byte-ring kernel takes a biased problem: its bias rows must
+// be whole 16-byte-aligned runs that bulk copies can move.
+bool mask_ring_supports(const RbfProblem& p) {
+  if (p.bias == nullptr) return false;
+  int es = 0;
+  if (p.bias_dtype == VECTRA_F32) es = 4;
+  if (p.bias_dtype == VECTRA_F16 || p.bias_dtype == VECTRA_BF16) es = 2;
+  if (es == 0) return false;
+  if (p.Nk > 1 && p.sb[2] != 1) return false;
+  if ((reinterpret_cast<uintptr_t>(p.bias) & 15u) != 0) return false;
+  if ((p.sb[0] * es) % 16 || (p.sb[1] * es) % 16) return false;
+  if ((p.Nk * es) % 16) return false;
+  return true;
+}
+
+template <typename T, int D, int DV>
+struct MaskLauncher {
+  static constexpr int KC =
+      kMaskItemBytes / ((D + DV) * int(sizeof(T))) >= 128
+          ? 128
+          : (kMaskItemBytes / ((D + DV) * int(sizeof(T))) >= 64 ? 64 : 32);
+  using Cfg = DecodeCfg<T, D, DV, KC>;
+  static constexpr int WARPS = VECTRA_MASK_WARPS;
+
+  static cudaError_t launch(const RbfProblem& p, cudaStream_t stream) {
+    const size_t budget = 227 * 1024;
+    const int bias_es = p.bias_dtype == VECTRA_F32 ? 4 : 2;
+    const size_t meta = size_t(kMaskSlots) * (8 + 8 + 16 + 4);
+    const size_t stage = size_t(kMaskSlots) * KC * bias_es;
+    const size_t warps_b = size_t(WARPS) * Cfg::WARP_BYTES;
+    const size_t ring =
+        (budget - meta - stage - warps_b - 256) & ~size_t(127);
+    // Each producer's quarter of the ring must hold a full item.
+    if (ring / kMaskProducers <
+        size_t(Cfg::QB + KC * (D + DV) * Cfg::ES + 256))
+      return cudaErrorInvalidConfiguration;
+    MaskLaunch L;
+    L.n_planes = static_cast<int>(p.B * p.H);
+    L.H = static_cast<int>(p.H);
+    L.nchunks = static_cast<int>((p.Nk + KC - 1) / KC);
+    L.k_contig = p.sk[2] == D;
+    L.v_contig = p.sv[2] == DV;
+    L.bias_es = bias_es;
+    L.bias_row = KC * bias_es;
+    L.ring_bytes = static_cast<int>(ring);
+    L.stage_area = static_cast<int>((ring + meta + 127) & ~size_t(127));
+    L.warp_area = L.stage_area + static_cast<int>(stage);
+    const size_t smem = size_t(L.warp_area) + warps_b;
+    int64_t blocks = L.n_planes;
+    const int64_t cap = device_sm_count();
+    if (blocks > cap) blocks = cap;
+    auto kern = rbf_decode_masked_kernel<T, D, DV, KC, WARPS>;
+    static std::atomic<int> configured[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    if (dev < 0 || dev >= 64 || !configured[dev].load()) {
+      cudaError_t err = cudaFuncSetAttribute(
+          kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          static_cast<int>(smem));
+      if (err != cudaSuccess) return err;
+      if (dev >= 0 && dev < 64) configured[dev].store(1);
+    }
+    return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)),
+                      dim3((WARPS + kMaskProducers) * 32), smem, stream, p,
+                      L);
+  }
+};
+
 // Small stages while a plane fits in two of them, else large stages.
 template <typename T, int D, int DV>
 cudaError_t launch_profile(const RbfProblem& p, cudaStream_t stream) {
   using Small = DecodeLauncher<T, D, DV, kSmallStageBytes, kSmallStageWarps>;
   using Large = DecodeLauncher<T, D, DV, kLargeStageBytes, kLargeStageWarps>;
+  if (VECTRA_DECODE_MASK_RING && mask_ring_supports(p))
+    return MaskLauncher<T, D, DV>::launch(p, stream);
   if (p.Nk <= 2 * Small::KC) return Small::launch(p, stream);
   return Large::launch(p, stream);
 }
