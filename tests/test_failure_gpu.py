@@ -51,6 +51,10 @@ def _describe(t):
 
 CASES = {
     'decode': ((6, 3, 1, 70, 64), 'bf16', True),
+    # Bias rows of 72 and 200 float32 keys are whole 16-byte runs: the
+    # byte-ring kernel for biased problems (one and two chunks per plane).
+    'decode_masked': ((6, 3, 1, 72, 64), 'bf16', True),
+    'decode_masked_2chunks': ((5, 2, 1, 200, 64), 'bf16', True),
     'small': ((3, 2, 33, 65, 32), 'bf16', True),
     'tc': ((1, 2, 300, 200, 64), 'bf16', True),
     'generic': ((2, 3, 21, 37, 48), 'f32', True),
@@ -85,7 +89,10 @@ def test_output_guard_bands_are_untouched(kernel):
     a.out = out.data_ptr()
     for i in range(4):
         a.out_stride[i] = out.stride(i)
-    a.flags = {'decode': _lib.FLAG_FORCE_DECODE, 'small': _lib.FLAG_FORCE_SMALL,
+    a.flags = {'decode': _lib.FLAG_FORCE_DECODE,
+               'decode_masked': _lib.FLAG_FORCE_DECODE,
+               'decode_masked_2chunks': _lib.FLAG_FORCE_DECODE,
+               'small': _lib.FLAG_FORCE_SMALL,
                'tc': _lib.FLAG_FORCE_TC, 'generic': _lib.FLAG_FORCE_GENERIC,
                'decode_mma': _lib.FLAG_FORCE_DECODE_MMA}[kernel]
     assert _lib.LIB.vectra_rbf_select_kernel(ctypes.byref(a)) >= 0, kernel
