@@ -1,6 +1,7 @@
 """Builds the two shared libraries of vectra_b200, in-tree.
 
-* libvectra_rbf.so: the CUDA kernels and the C ABI (include/vectra_rbf.h),
+* libvectra_rbf.so: the CUDA kernels and the C ABI (include/vectra_rbf.h
+  and include/vectra_scan.h),
   compiled by nvcc for sm_100a only. No torch dependency.
 * _vectra_rbf_torch.so: the PyTorch binding that registers the CUDA kernel
   of vectra::rbf_attention; links libvectra_rbf.so through $ORIGIN.
@@ -32,7 +33,7 @@ TORCH_EXT = os.path.join(PKG, '_vectra_rbf_torch.so')
 
 CU_SOURCES = ['capi.cu', 'rbf_generic.cu', 'rbf_decode.cu',
               'rbf_decode_mma.cu', 'rbf_tc.cu', 'rbf_small.cu',
-              'tma_maps.cu']
+              'tma_maps.cu', 'scan.cu']
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 
