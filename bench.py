@@ -77,9 +77,14 @@ def parse_args(argv=None):
     p.add_argument('--model', action='store_true',
                    help='config 5 only: the whole compiled model served from '
                         'CUDA graphs (predictions/s) instead of one site')
+    p.add_argument('--scan', choices=('l2', 'pq'),
+                   help='the index-shard scan path instead of the operator: '
+                        'exhaustive L2 or PQ top-k (queries/s)')
     args = p.parse_args(argv)
     if args.model and args.config != 5:
         p.error('--model needs --config 5')
+    if args.scan and args.model:
+        p.error('--scan and --model are separate workloads')
     return args
 
 
@@ -830,6 +835,279 @@ def run_model(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# The index-shard scan path (--scan l2|pq)
+# ---------------------------------------------------------------------------
+
+# Queries per step: a CTA's group of 8 for L2 (the distances stay under the
+# HBM time), one for PQ (its table lookups grow with the queries and would
+# outrun the 256 MB of codes).
+SCAN_QUERIES = {'l2': 8, 'pq': 1}
+SCAN_K = 64          # the reference's rerank_depth default
+SCAN_L2 = dict(rows=1 << 20, dim=128)          # 512 MB of float32 rows
+SCAN_PQ = dict(rows=1 << 24, subspaces=16)     # 256 MB of codes
+
+
+def scan_metric(kind):
+    if kind == 'l2':
+        return (f'exhaustive L2 top-{SCAN_K} scan queries/s (shard of '
+                f'{SCAN_L2["rows"]:,} rows x {SCAN_L2["dim"]} float32, '
+                f'{SCAN_QUERIES["l2"]} queries per step)', 'queries/s')
+    return (f'PQ-ADC top-{SCAN_K} scan queries/s (shard of '
+            f'{SCAN_PQ["rows"]:,} codes x {SCAN_PQ["subspaces"]} bytes, '
+            f'{SCAN_QUERIES["pq"]} query per step)', 'queries/s')
+
+
+def scan_inputs(kind, seed=0):
+    """Seeded host arrays of the scan workload (rows or codes, queries or
+    tables)."""
+    rng = np.random.default_rng(seed)
+    if kind == 'l2':
+        rows = rng.standard_normal((SCAN_L2['rows'], SCAN_L2['dim']),
+                                   dtype=np.float32)
+        queries = rng.standard_normal((4 * SCAN_QUERIES['l2'],
+                                       SCAN_L2['dim']), dtype=np.float32)
+        return rows, queries
+    codes = rng.integers(0, 256, (SCAN_PQ['rows'], SCAN_PQ['subspaces']),
+                         dtype=np.uint8)
+    tables = (rng.random((4 * SCAN_QUERIES['pq'], SCAN_PQ['subspaces'], 256),
+                         dtype=np.float32) * 4)
+    return codes, tables
+
+
+def time_scan_cpu(kind, data, queries, seconds, threads):
+    """The reference's scan on the host: ExhaustiveSearch's bounded top-k
+    over L2SquaredDistance / PqAdcDistance from oracle/_ref (the reference
+    engine's own sources) when built, else the NumPy port; one query per
+    thread over a bounded sample of the shard. (queries/s, cores, kind,
+    sample)."""
+    from oracle import scan_oracle  # pylint: disable=import-outside-toplevel
+    ref = scan_oracle.load_reference(fast=True) or scan_oracle.load_reference()
+    n_sample = min(data.shape[0], 1 << 18)
+    sample = np.ascontiguousarray(data[:n_sample])
+    if ref is not None:
+        one = ((lambda q: ref.exhaustive_topk(q, sample, SCAN_K))
+               if kind == 'l2' else
+               (lambda q: ref.pq_topk(q, sample, SCAN_K)))
+        kind_name = 'reference'
+    else:
+        one = ((lambda q: scan_oracle.exhaustive_l2_topk(q, sample, SCAN_K))
+               if kind == 'l2' else
+               (lambda q: scan_oracle.pq_topk(q, sample, SCAN_K)))
+        kind_name = 'port'
+    scale = data.shape[0] / n_sample  # full-shard queries per sampled query
+    with concurrent.futures.ThreadPoolExecutor(threads) as pool:
+        list(pool.map(one, [queries[i % len(queries)]
+                            for i in range(threads)]))  # warm-up
+        t0 = time.perf_counter()
+        done = 0
+        while done == 0 or time.perf_counter() - t0 < seconds:
+            list(pool.map(one, [queries[(done + i) % len(queries)]
+                                for i in range(threads)]))
+            done += threads
+        elapsed = time.perf_counter() - t0
+    sample_txt = (f'{kind_name}: one query per thread over the first '
+                  f'{n_sample:,} rows of the shard ({done} queries), scaled '
+                  f'to the full shard')
+    return done / scale / elapsed, threads, kind_name, sample_txt
+
+
+def run_scan_reference(args):
+    if int(os.environ.get('RANK', '0')) != 0:
+        return 0
+    sys.path.insert(0, ROOT)
+    metric, unit = scan_metric(args.scan)
+    data, queries = scan_inputs(args.scan)
+    threads = os.cpu_count() or 1
+    per_step = max(0.2, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        time_scan_cpu(args.scan, data, queries, per_step / 4, threads)
+    runs = [time_scan_cpu(args.scan, data, queries, per_step, threads)
+            for _ in range(args.steps)]
+    value = float(statistics.median(r[0] for r in runs))
+    _, cores, kind, sample = runs[0]
+    emit({
+        'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
+        'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'f32', 'data': 'synthetic (seeded)',
+        'config': {'workload': f'scan {args.scan}', 'device': 'host CPU',
+                   'threads': cores},
+        'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
+                         'kind': kind, 'sample': sample,
+                         'cpu_model': cpu_model()},
+        'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
+                'd2h_bytes_per_step': 0},
+    })
+    return 0
+
+
+def run_scan(args):
+    """The shard (rows or PQ codes) resident in HBM; one step = one call of
+    the scan over SCAN_QUERIES queries, through the C ABI with the argument
+    block prepared once (queries rotate over four sets). The shard (> L2)
+    is read from HBM by every step. e2e: the same with the step's queries
+    copied in from pinned host memory and its results read back."""
+    import ctypes  # pylint: disable=import-outside-toplevel
+    import torch  # pylint: disable=import-outside-toplevel
+    import torch.distributed as dist  # pylint: disable=import-outside-toplevel
+    sys.path.insert(0, ROOT)
+    from vectra_b200 import _lib  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import scan  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    distributed = world > 1
+    if distributed:
+        import datetime  # pylint: disable=import-outside-toplevel
+        dist.init_process_group('nccl', device_id=dev,
+                                timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if distributed:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    data_h, queries_h = scan_inputs(args.scan, seed=rank)
+    data = torch.from_numpy(data_h).to(dev)
+    queries = torch.from_numpy(queries_h).to(dev)
+    nq, k = SCAN_QUERIES[args.scan], SCAN_K
+    ws = torch.empty(scan.workspace_bytes(nq, data.shape[0], k),
+                     dtype=torch.uint8, device=dev)
+    out_d = torch.empty(nq, k, dtype=torch.float32, device=dev)
+    out_n = torch.empty(nq, k, dtype=torch.int32, device=dev)
+    counts = torch.empty(nq, dtype=torch.int32, device=dev)
+    res = scan.Results(out_d.data_ptr(), out_n.data_ptr(), counts.data_ptr())
+    cand = scan.Candidates(None, None, 0)
+    if args.scan == 'l2':
+        alg_bytes = data.numel() * 4 + nq * data.shape[1] * 4 + nq * k * 8
+        blocks = [scan.L2Args(queries[i * nq].data_ptr(), nq,
+                              queries.stride(0), data.data_ptr(),
+                              data.shape[0], data.stride(0), data.shape[1],
+                              k, cand, res, ws.data_ptr(), ws.numel())
+                  for i in range(4)]
+        call = _lib.LIB.vectra_scan_l2_topk
+    else:
+        alg_bytes = data.numel() + nq * queries[0].numel() * 4 + nq * k * 8
+        blocks = [scan.PqArgs(queries[i * nq].data_ptr(), nq, data.data_ptr(),
+                              data.shape[0], data.stride(0), data.shape[1], k,
+                              cand, res, ws.data_ptr(), ws.numel())
+                  for i in range(4)]
+        call = _lib.LIB.vectra_scan_pq_topk
+    stream = torch.cuda.current_stream(dev)
+    handle = ctypes.c_void_p(stream.cuda_stream)
+    # Sample pass, its bounds, the main pass and the merge when the shard
+    # spans several 4,096-candidate tiles.
+    launches_per_step = 4 if data.shape[0] > 4096 else 2
+
+    def step(i):
+        status = call(ctypes.byref(blocks[i % 4]), handle)
+        if status != _lib.OK:
+            raise RuntimeError(_lib.strerror(status))
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    if args.profile:
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        if distributed:
+            dist.destroy_process_group()
+        return 0
+    sampler = ClockSampler(local)
+    t_soak = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_soak < 0.6:
+        step(i)
+        i += 1
+        if i % 16 == 0:
+            torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    region_ms = e0.elapsed_time(e1)
+    ms_per_step = sharding.max_over_ranks(region_ms, device=dev) / args.steps
+    value = nq * world / (ms_per_step * 1e-3)
+
+    # End to end: each step's queries (or tables) from pinned host memory
+    # into the argument block's buffer, the results back to pinned host
+    # memory.
+    q_host = torch.from_numpy(queries_h[:nq]).pin_memory()
+    d_host = torch.empty_like(out_d, device='cpu').pin_memory()
+    n_host = torch.empty_like(out_n, device='cpu').pin_memory()
+    h2d = q_host.numel() * q_host.element_size()
+    d2h = (d_host.numel() * d_host.element_size() +
+           n_host.numel() * n_host.element_size())
+    target = queries[:nq]
+    e2e_steps = max(3, min(args.e2e_steps, args.steps))
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        target.copy_(q_host, non_blocking=True)
+        step(0)
+        d_host.copy_(out_d, non_blocking=True)
+        n_host.copy_(out_n, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = sharding.max_over_ranks(f0.elapsed_time(f1),
+                                     device=dev) / e2e_steps
+    hbm, _, peak_kind = peaks()
+    achieved = alg_bytes / (ms_per_step * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, kind, sample = time_scan_cpu(args.scan, data_h, queries_h,
+                                               args.cpu_seconds,
+                                               os.cpu_count() or 1)
+        cpu = {'value': v, 'unit': 'queries/s', 'cores': cores, 'kind': kind,
+               'sample': sample, 'cpu_model': cpu_model()}
+    if rank == 0:
+        metric, unit = scan_metric(args.scan)
+        emit({
+            'metric': metric, 'value': value, 'unit': unit, 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms_per_step, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded)',
+            'config': {
+                'workload': f'scan {args.scan}: one shard per GPU, '
+                            f'{nq} queries per step, k = {k}',
+                'shard_bytes': data.numel() * data.element_size(),
+                'l2': 'shard > L2, read from HBM every step',
+                'parallelism': f'a shard per GPU x{world}, no collective',
+            },
+            'e2e': {'value': nq * world / (e2e_ms * 1e-3), 'unit': unit,
+                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                    'steps': e2e_steps},
+            'gpu_launches': launches_per_step * args.steps,
+            'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
+                         'unit': 'GB/s', 'frac': achieved / hbm,
+                         'traffic': None,
+                         'peak_kind': f'HBM copy, {peak_kind}',
+                         'algorithmic_bytes_per_launch': alg_bytes,
+                         'kernel': 'sample, bound, scan and merge launches '
+                                   'per step'},
+            'cpu_baseline': cpu,
+            'clocks': clocks,
+        })
+    if distributed:
+        dist.destroy_process_group()
+    return 0
+
+
 # The JSON line goes to the process's original standard output; while the
 # benchmark runs, file descriptor 1 points at standard error, so that what
 # libraries print there (NCCL's version banner, for one) cannot come before
@@ -852,8 +1130,12 @@ def main(argv=None):
         _RESULT_OUT = os.fdopen(os.dup(saved), 'w')
         os.dup2(2, 1)
         if args.impl == 'reference':
+            if args.scan:
+                return run_scan_reference(args)
             return (run_model_reference(args) if args.model
                     else run_reference(args))
+        if args.scan:
+            return run_scan(args)
         return run_model(args) if args.model else run_vectra(args)
     finally:
         sys.stdout.flush()

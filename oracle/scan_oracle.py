@@ -31,8 +31,10 @@ import numpy as np
 
 LANES = 16
 CENTROIDS = 256
-REF_LIB = os.path.join(os.path.dirname(os.path.abspath(__file__)), '_ref',
-                       'libvectra_engine_ref.so')
+REF_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), '_ref')
+REF_LIB = os.path.join(REF_DIR, 'libvectra_engine_ref.so')
+# The same sources with the reference's Release flags (the timed baseline).
+REF_FAST_LIB = os.path.join(REF_DIR, 'libvectra_engine_ref_fast.so')
 
 
 def l2_squared(query: np.ndarray, rows: np.ndarray) -> np.ndarray:
@@ -217,9 +219,15 @@ class Reference:
         return out
 
 
-def load_reference():
-    """The compiled reference, or None when oracle/_ref has not been built
-    (it needs the reference sources; see oracle/Makefile)."""
-    if not os.path.exists(REF_LIB):
+def load_reference(fast: bool = False):
+    """The compiled reference (the checker build, or with fast=True the
+    Release build that bench.py times), or None when oracle/_ref has not
+    been built (it needs the reference sources; see oracle/Makefile) or
+    cannot load on this host."""
+    path = REF_FAST_LIB if fast else REF_LIB
+    if not os.path.exists(path):
         return None
-    return Reference()
+    try:
+        return Reference(path)
+    except OSError:
+        return None
