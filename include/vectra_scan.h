@@ -104,6 +104,17 @@ VECTRA_API int vectra_scan_l2_topk(const vectra_scan_l2_args* args,
 VECTRA_API int vectra_scan_pq_topk(const vectra_scan_pq_args* args,
                                    void* stream);
 
+/* vectra_scan_l2_topk without a caller workspace: the scan's scratch is a
+ * static array of VECTRA_SCAN_NOALLOC_SCRATCH_BYTES in the library's device
+ * memory, one per device, looked up once per device; calls on one device
+ * take turns with it (each waits for the previous call's kernels, on any
+ * stream). args->workspace is ignored. VECTRA_ERR_UNSUPPORTED when the scan
+ * needs more scratch than that (vectra_scan_workspace_bytes).
+ * No counterpart in the reference: an entry point of this library only. */
+#define VECTRA_SCAN_NOALLOC_SCRATCH_BYTES (8u << 20)
+VECTRA_API int vectra_scan_l2_topk_noalloc(const vectra_scan_l2_args* args,
+                                           void* stream);
+
 /* tables[q][s][c] = squared L2 distance from sub-vector s of query q to
  * centroid c of sub-space s; codebooks laid out [subspace][centroid]
  * [dimension / subspaces] as ProductQuantizer stores them

@@ -270,7 +270,8 @@ const char* vectra_rbf_strerror(int status) {
     case VECTRA_ERR_BIAS_QUERY:
       return "key_bias must be constant across queries";
     case VECTRA_ERR_UNSUPPORTED:
-      return "head widths above 512 are not supported";
+      return "unsupported size: a head width above 512, a scan's k above "
+             "256, or a scan larger than the static scan scratch";
     case VECTRA_ERR_CUDA:
       return "a CUDA runtime call failed";
     case VECTRA_ERR_DEVICE:

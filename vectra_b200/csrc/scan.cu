@@ -878,6 +878,28 @@ int prepare(int64_t n_queries, int64_t n_rows, int k,
 }  // namespace scan
 }  // namespace vectra
 
+// Scratch of vectra_scan_l2_topk_noalloc: one array per device context, in
+// the module's global memory (no allocation at call time). Its address is
+// looked up once per device; calls on one device take turns with it.
+static __device__ __align__(256) unsigned char
+    g_scan_scratch[size_t(VECTRA_SCAN_NOALLOC_SCRATCH_BYTES)];
+
+namespace vectra {
+namespace scan {
+namespace {
+
+struct StaticScratch {
+  void* ptr = nullptr;
+  cudaEvent_t last_use = nullptr;  // the previous call's work on it
+};
+
+std::mutex g_scratch_mu;
+StaticScratch g_scratch[64];
+
+}  // namespace
+}  // namespace scan
+}  // namespace vectra
+
 using namespace vectra::scan;  // NOLINT
 
 extern "C" {
@@ -933,6 +955,42 @@ VECTRA_API int vectra_scan_pq_topk(const vectra_scan_pq_args* a,
                 a->subspaces * VECTRA_PQ_CENTROIDS, run) == cudaSuccess
              ? VECTRA_OK
              : VECTRA_ERR_CUDA;
+}
+
+VECTRA_API int vectra_scan_l2_topk_noalloc(const vectra_scan_l2_args* a,
+                                           void* stream) {
+  if (a == nullptr) return VECTRA_ERR_NULL;
+  if (a->k < 1 || a->k > VECTRA_SCAN_MAX_K) return VECTRA_ERR_UNSUPPORTED;
+  const int64_t nc = a->candidates.offsets == nullptr
+                         ? a->n_rows
+                         : a->candidates.max_per_query;
+  if (a->n_queries < 0 || nc < 0) return VECTRA_ERR_SHAPE;
+  if (workspace_for(a->n_queries, nc, a->k) >
+      size_t(VECTRA_SCAN_NOALLOC_SCRATCH_BYTES))
+    return VECTRA_ERR_UNSUPPORTED;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return VECTRA_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  StaticScratch& ss = g_scratch[dev];
+  if (ss.ptr == nullptr) {
+    if (cudaGetSymbolAddress(&ss.ptr, g_scan_scratch) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.last_use, cudaEventDisableTiming) !=
+            cudaSuccess) {
+      ss.ptr = nullptr;
+      return VECTRA_ERR_CUDA;
+    }
+  }
+  vectra_scan_l2_args b = *a;
+  b.workspace = ss.ptr;
+  b.workspace_bytes = size_t(VECTRA_SCAN_NOALLOC_SCRATCH_BYTES);
+  // After the previous call's kernels, whatever stream they ran on.
+  if (cudaStreamWaitEvent(s, ss.last_use, 0) != cudaSuccess)
+    return VECTRA_ERR_CUDA;
+  const int status = vectra_scan_l2_topk(&b, stream);
+  if (cudaEventRecord(ss.last_use, s) != cudaSuccess) return VECTRA_ERR_CUDA;
+  return status;
 }
 
 VECTRA_API int vectra_pq_distance_tables(const float* queries,

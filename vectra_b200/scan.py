@@ -36,9 +36,12 @@ CENTROIDS = 256
 EXPORTED = (
     'vectra_scan_workspace_bytes',
     'vectra_scan_l2_topk',
+    'vectra_scan_l2_topk_noalloc',
     'vectra_scan_pq_topk',
     'vectra_pq_distance_tables',
 )
+# Scratch of vectra_scan_l2_topk_noalloc (VECTRA_SCAN_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 class Candidates(ctypes.Structure):
@@ -82,6 +85,9 @@ def _bind(lib):
     lib.vectra_scan_l2_topk.argtypes = [ctypes.POINTER(L2Args),
                                         ctypes.c_void_p]
     lib.vectra_scan_l2_topk.restype = ctypes.c_int
+    lib.vectra_scan_l2_topk_noalloc.argtypes = [ctypes.POINTER(L2Args),
+                                                ctypes.c_void_p]
+    lib.vectra_scan_l2_topk_noalloc.restype = ctypes.c_int
     lib.vectra_scan_pq_topk.argtypes = [ctypes.POINTER(PqArgs),
                                         ctypes.c_void_p]
     lib.vectra_scan_pq_topk.restype = ctypes.c_int
@@ -163,8 +169,16 @@ def _workspace(nbytes, device, workspace):
     return workspace
 
 
+def l2_topk_noalloc(queries: torch.Tensor, rows: torch.Tensor, k: int,
+                    candidates=None):
+    """l2_topk through vectra_scan_l2_topk_noalloc: no workspace (the
+    library's static scratch; calls on one device take turns with it)."""
+    return l2_topk(queries, rows, k, candidates, _noalloc=True)
+
+
 def l2_topk(queries: torch.Tensor, rows: torch.Tensor, k: int,
-            candidates=None, workspace: torch.Tensor | None = None):
+            candidates=None, workspace: torch.Tensor | None = None,
+            _noalloc: bool = False):
     """The k rows nearest to each query (squared L2), sorted by (distance,
     node): (distances [Q, k] float32, nodes [Q, k] int32, counts [Q]).
 
@@ -184,12 +198,20 @@ def l2_topk(queries: torch.Tensor, rows: torch.Tensor, k: int,
     nq, d = queries.shape
     cand, keep, mx = _candidates(candidates, nq, queries.device)
     dist, nodes, counts, res = _results(nq, k, queries.device)
+    stream = torch.cuda.current_stream(queries.device).cuda_stream
+    if _noalloc:
+        a = L2Args(queries.data_ptr(), nq, queries.stride(0), rows.data_ptr(),
+                   rows.shape[0], rows.stride(0), d, k, cand, res, None, 0)
+        _check(_lib.LIB.vectra_scan_l2_topk_noalloc(
+            ctypes.byref(a), ctypes.c_void_p(stream)),
+               'vectra_scan_l2_topk_noalloc')
+        del keep
+        return dist, nodes, counts
     need = workspace_bytes(nq, rows.shape[0] if mx is None else mx, k)
     ws = _workspace(need, queries.device, workspace)
     a = L2Args(queries.data_ptr(), nq, queries.stride(0), rows.data_ptr(),
                rows.shape[0], rows.stride(0), d, k, cand, res, ws.data_ptr(),
                ws.numel() * ws.element_size())
-    stream = torch.cuda.current_stream(queries.device).cuda_stream
     _check(_lib.LIB.vectra_scan_l2_topk(ctypes.byref(a),
                                         ctypes.c_void_p(stream)),
            'vectra_scan_l2_topk')
