@@ -104,12 +104,23 @@ VECTRA_API int vectra_scan_l2_topk(const vectra_scan_l2_args* args,
 VECTRA_API int vectra_scan_pq_topk(const vectra_scan_pq_args* args,
                                    void* stream);
 
-/* vectra_scan_l2_topk without a caller workspace: the scan's scratch is a
- * static array of VECTRA_SCAN_NOALLOC_SCRATCH_BYTES in the library's device
- * memory, one per device, looked up once per device; calls on one device
- * take turns with it (each waits for the previous call's kernels, on any
- * stream). args->workspace is ignored. VECTRA_ERR_UNSUPPORTED when the scan
- * needs more scratch than that (vectra_scan_workspace_bytes).
+/* vectra_scan_l2_topk for callers that cannot allocate device memory: a
+ * host bound through an FFI (cgo, JNI, ctypes) that is handed device
+ * pointers but has no CUDA allocator of its own, or a serving loop that
+ * allows no cudaMalloc after start-up (it synchronizes the device and can
+ * fail under memory pressure). The caller passes inputs and outputs only;
+ * the scan's scratch is a static array of VECTRA_SCAN_NOALLOC_SCRATCH_BYTES
+ * (8 MB) built into the library, which every GPU that loads the library
+ * holds until the process exits. args->workspace is ignored.
+ * VECTRA_ERR_UNSUPPORTED when the scan needs more scratch than that
+ * (vectra_scan_workspace_bytes above VECTRA_SCAN_NOALLOC_SCRATCH_BYTES).
+ * The first call on a device, with that device current, looks up the
+ * array's device address and creates one event: make it before any stream
+ * capture. Every call on a device shares the array, and two calls in
+ * flight on the GPU at once would race on it, so each call's stream first
+ * waits for the previous call's kernels, whatever stream they ran on. A
+ * call writes every part of the array that it reads; nothing carries over
+ * from the last call.
  * No counterpart in the reference: an entry point of this library only. */
 #define VECTRA_SCAN_NOALLOC_SCRATCH_BYTES (8u << 20)
 VECTRA_API int vectra_scan_l2_topk_noalloc(const vectra_scan_l2_args* args,

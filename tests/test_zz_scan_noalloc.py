@@ -1,10 +1,14 @@
-"""vectra_scan_l2_topk_noalloc: the L2 scan with its scratch in a static
-device array of the library (no workspace from the caller, no allocation).
+"""vectra_scan_l2_topk_noalloc: the L2 scan for callers that cannot allocate
+device memory (an FFI host handed device pointers with no CUDA allocator of
+its own, or a serving loop that forbids cudaMalloc after start-up). Its
+scratch is a static device array of the library; the caller passes only
+inputs and outputs.
 
-Its results must equal vectra_scan_l2_topk's with a caller workspace bit for
-bit (the same kernels run), calls issued on different streams must not share
-the scratch at the same time, and a scan needing more scratch than the array
-holds is refused with VECTRA_ERR_UNSUPPORTED.
+Called through the C ABI, its results must equal vectra_scan_l2_topk's with
+a caller workspace bit for bit (the same kernels run) on calls in a row,
+calls issued on different streams must not share the scratch at the same
+time, and a scan needing more scratch than the array holds is refused with
+VECTRA_ERR_UNSUPPORTED. This file is collected last and also passes alone.
 """
 
 import numpy as np
@@ -41,8 +45,12 @@ def test_null_arguments_need_no_gpu():
                                       (11, 20000, 64, 256), (5, 6000, 129, 33)])
 def test_equals_the_workspace_entry_point(nq, n, d, k):
     queries, rows = _inputs(nq, n, d, seed=nq * 100 + k)
-    _same(scan.l2_topk_noalloc(queries, rows, k), scan.l2_topk(queries, rows,
-                                                               k))
+    other = (queries.flip(0) + 0.5).contiguous()
+    # Two calls in a row: the second must not see the first one's scratch.
+    first = scan.l2_topk_noalloc(queries, rows, k)
+    second = scan.l2_topk_noalloc(other, rows, k)
+    _same(first, scan.l2_topk(queries, rows, k))
+    _same(second, scan.l2_topk(other, rows, k))
 
 
 @pytest.mark.gpu
@@ -80,6 +88,9 @@ def test_scans_beyond_the_static_scratch_are_refused():
     assert scan.workspace_bytes(64, 1 << 20, 64) > scan.NOALLOC_SCRATCH_BYTES
     with pytest.raises(scan.ScanError, match='unsupported'):
         scan.l2_topk_noalloc(queries, rows, 64)
-    half = queries[:32].contiguous()
-    assert scan.workspace_bytes(32, 1 << 20, 64) <= scan.NOALLOC_SCRATCH_BYTES
-    _same(scan.l2_topk_noalloc(half, rows, 64), scan.l2_topk(half, rows, 64))
+    # The most queries (of 32 at most) whose scan fits the scratch.
+    fit = max(nq for nq in (1, 2, 4, 8, 16, 32)
+              if scan.workspace_bytes(nq, 1 << 20, 64) <=
+              scan.NOALLOC_SCRATCH_BYTES)
+    part = queries[:fit].contiguous()
+    _same(scan.l2_topk_noalloc(part, rows, 64), scan.l2_topk(part, rows, 64))

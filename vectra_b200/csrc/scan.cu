@@ -878,9 +878,12 @@ int prepare(int64_t n_queries, int64_t n_rows, int k,
 }  // namespace scan
 }  // namespace vectra
 
-// Scratch of vectra_scan_l2_topk_noalloc: one array per device context, in
-// the module's global memory (no allocation at call time). Its address is
-// looked up once per device; calls on one device take turns with it.
+// Scratch of vectra_scan_l2_topk_noalloc, for callers that cannot allocate:
+// one array per device context in the module's global memory, held until
+// the process exits. In host code its name is only a stand-in; the device
+// address is looked up once per device (cudaGetSymbolAddress, that device
+// current) and passed to the kernels. Calls on one device take turns with
+// it (an event per device), since overlapping calls would race on it.
 static __device__ __align__(256) unsigned char
     g_scan_scratch[size_t(VECTRA_SCAN_NOALLOC_SCRATCH_BYTES)];
 
