@@ -912,6 +912,24 @@ def time_scan_cpu(kind, data, queries, seconds, threads):
     return done / scale / elapsed, threads, kind_name, sample_txt
 
 
+def scan_launches(n_cand, k):
+    """Kernel launches of one scan call: a level kernel and a select per
+    level, plus the warp-list re-scan's two (which return at once unless a
+    query's last level overflowed). Mirrors the level plan in
+    vectra_b200/csrc/scan.cu (plan_for)."""
+    cap, sample0 = 32768, 8192
+    if n_cand <= cap:
+        return 2
+    levels, s = 1, sample0
+    while levels < 6 and k * n_cand > (cap // 4) * s:
+        s2 = s * (cap // 8) // k
+        if 2 * s2 >= n_cand:
+            break
+        levels += 1
+        s = s2
+    return 2 * (levels + 1) + 2
+
+
 def run_scan_reference(args):
     if int(os.environ.get('RANK', '0')) != 0:
         return 0
@@ -1002,7 +1020,7 @@ def run_scan(args):
     handle = ctypes.c_void_p(stream.cuda_stream)
     # Sample pass, its bounds, the main pass and the merge when the shard
     # spans several 4,096-candidate tiles.
-    launches_per_step = 4 if data.shape[0] > 4096 else 2
+    launches_per_step = scan_launches(data.shape[0], SCAN_K)
 
     def step(i):
         status = call(ctypes.byref(blocks[i % 4]), handle)
@@ -1098,8 +1116,8 @@ def run_scan(args):
                          'traffic': None,
                          'peak_kind': f'HBM copy, {peak_kind}',
                          'algorithmic_bytes_per_launch': alg_bytes,
-                         'kernel': 'sample, bound, scan and merge launches '
-                                   'per step'},
+                         'kernel': 'every launch of a step (sample and '
+                                   'full levels, selects, re-scan check)'},
             'cpu_baseline': cpu,
             'clocks': clocks,
         })

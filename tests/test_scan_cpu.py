@@ -103,7 +103,8 @@ def test_workspace_bytes():
     small = scan.workspace_bytes(8, 4096, 64)
     assert small > 0
     assert scan.workspace_bytes(8, 1 << 20, 64) > small
-    assert scan.workspace_bytes(8, 4096, 256) > small
+    big = scan.workspace_bytes(8, 1 << 20, 64)
+    assert scan.workspace_bytes(8, 1 << 20, 256) > big  # re-scan lists
     for bad in ((8, 4096, 0), (8, 4096, 257), (-1, 10, 4), (2, -1, 4)):
         assert scan.workspace_bytes(*bad) == 0
 

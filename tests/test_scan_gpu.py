@@ -205,3 +205,94 @@ def test_results_are_deterministic_and_use_the_launching_stream():
     b = scan.l2_topk(queries, rows, 64)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+# Scans of more than 32,768 candidates run in levels: a sample's k-th
+# distance bounds the next level, whose select keeps the k nearest of the
+# few candidates under it; a last level that admits more than its buffer
+# holds (mass ties) is redone by the warp-list scan. The cases below reach
+# each of these.
+
+def _pq_check(tables, codes, k, cands=None):
+    gd, gn, gc = scan.pq_topk(torch.from_numpy(tables).cuda(),
+                              torch.from_numpy(codes).cuda(), k, cands)
+    for qi in range(tables.shape[0]):
+        ids = None if cands is None else cands[qi]
+        wd, wn = scan_oracle.pq_topk(tables[qi], codes, k, ids)
+        cnt = wd.shape[0]
+        assert int(gc[qi]) == cnt
+        np.testing.assert_array_equal(gd[qi, :cnt].cpu().numpy(), wd)
+        np.testing.assert_array_equal(
+            gn[qi, :cnt].cpu().numpy().astype(np.int64), wn)
+        assert np.all(gn[qi, cnt:].cpu().numpy() == -1)
+
+
+def test_pq_three_levels_bit_for_bit():
+    rng = np.random.default_rng(21)
+    tables = (rng.random((3, 8, 256)) * 3).astype(np.float32)
+    codes = rng.integers(0, 256, (1 << 20, 8), dtype=np.uint8)
+    _pq_check(tables, codes, 256)  # k = 256 over 1M codes: three levels
+
+
+def test_pq_ties_at_the_bound_across_levels():
+    rng = np.random.default_rng(22)
+    tables = np.floor(rng.random((4, 8, 256)) * 4).astype(np.float32)
+    codes = rng.integers(0, 256, (200000, 8), dtype=np.uint8)
+    _pq_check(tables, codes, 100)
+
+
+def test_pq_mass_ties_overflow_and_rescan():
+    codes = np.random.default_rng(23).integers(0, 256, (100000, 16),
+                                               dtype=np.uint8)
+    tables = np.ones((2, 16, 256), np.float32)  # every distance is 16
+    tables[1, 3, :] = 0.5  # and 15.5 for the second query
+    _pq_check(tables, codes, 50)
+
+
+def test_l2_identical_rows_overflow_and_rescan():
+    rows = np.tile(np.arange(16, dtype=np.float32), (60000, 1))
+    queries = np.zeros((3, 16), np.float32)
+    queries[1] = 1.0
+    gd, gn, gc = scan.l2_topk(torch.from_numpy(queries).cuda(),
+                              torch.from_numpy(rows).cuda(), 20)
+    for qi in range(3):
+        wd, wn = scan_oracle.exhaustive_l2_topk(queries[qi], rows, 20)
+        assert int(gc[qi]) == 20
+        np.testing.assert_array_equal(gn[qi].cpu().numpy().astype(np.int64),
+                                      wn)  # nodes 0..19: ties by node id
+        assert np.all(gd[qi].cpu().numpy() == gd[qi, 0].item())
+
+
+def test_l2_candidate_lists_of_every_size():
+    rng = np.random.default_rng(24)
+    n, d = 150000, 32
+    rows = rng.standard_normal((n, d)).astype(np.float32)
+    queries = (rows[:5] + 0.2 * rng.standard_normal((5, d))).astype(
+        np.float32)
+    cands = [np.zeros(0, np.int64), np.array([4, 17, 3]),
+             rng.choice(n, 40000, replace=False),
+             rng.choice(n, 120000, replace=False), np.arange(n)]
+    gd, gn, gc = scan.l2_topk(torch.from_numpy(queries).cuda(),
+                              torch.from_numpy(rows).cuda(), 64, cands)
+    gd, gn, gc = gd.cpu().numpy(), gn.cpu().numpy(), gc.cpu().numpy()
+    for qi in range(5):
+        wd, wn = scan_oracle.exhaustive_l2_topk(queries[qi], rows, 64,
+                                                cands[qi])
+        cnt = wd.shape[0]
+        assert gc[qi] == cnt
+        assert np.all(gn[qi, cnt:] == -1) and np.all(np.isinf(gd[qi, cnt:]))
+        if cnt:
+            _check_l2(gd[qi], gn[qi], cnt, wd, wn, queries[qi], rows, d)
+
+
+def test_duplicate_candidate_ids_are_kept_like_the_reference_heap():
+    # PushBounded (shard_index.cc:111-120) keeps the k smallest of the
+    # multiset: a repeated id appears as often as it is among them.
+    rng = np.random.default_rng(25)
+    tables = np.repeat((rng.random((1, 8, 256)) * 3).astype(np.float32), 3,
+                       axis=0)
+    codes = rng.integers(0, 256, (50000, 8), dtype=np.uint8)
+    best = int(np.argmin(scan_oracle.pq_adc(tables[0], codes)))
+    lists = [np.concatenate([np.full(copies, best), rng.choice(50000, 500)])
+             for copies in (7, 3000, 40000)]  # sorted, past the sort, re-scan
+    _pq_check(tables, codes, 30, lists)

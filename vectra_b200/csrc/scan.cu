@@ -4,40 +4,40 @@
 // L2SquaredDistance / PqAdcDistance (engine/src/index/simd_distance.cc) and
 // ProductQuantizer::ComputeDistanceTable (engine/src/index/pq_codec.cc).
 //
-// Design (B200):
-//  * Candidates are scanned in tiles of kTile = 4,096 by persistent CTAs of
-//    8 warps: for a group of QG queries (their vectors, or their PQ tables,
-//    in shared memory) a CTA takes tiles slot, slot + n_slots, ... (about
-//    two CTAs per SM over all groups). The CTAs of all query groups with the
-//    same slot run together and read each tile from HBM once (L2 serves
-//    the others).
-//  * An admission bound first: a sample pass scans each query's first tile
-//    and its k-th nearest there bounds the true k-th nearest from above
-//    (as a (distance, node) pair), so the main pass offers a warp's list
-//    only the candidates at or under it (about k of every tile's 4,096);
-//    without it every warp list would be filled from empty and insertions,
-//    not distances, would dominate.
-//  * Lane per candidate row: the lane reads its row with 16-byte loads
-//    (read-only path) and forms the distance to each of the QG queries:
-//    sum_d (q_d - r_d)^2 in float32 with packed f32x2 subtract/FMA (the
-//    reference formulation, direct differences); for PQ the sum of the
-//    table entries of its code bytes, in PqAdcDistance's order (four chains,
-//    (l0 + l1) + (l2 + l3), then the tail: bit-identical sums).
-//  * Top-k: each warp keeps, per query, a sorted list of k (distance, node)
-//    pairs spread over its lanes' registers (entry j at lane j % 32, slot
-//    j / 32), ordered as CloserFirst orders them (distance, then node id;
-//    engine/include/vectra/index/search_scratch.h:35-40). Each batch of 32
-//    candidates is filtered by the list's last entry (a ballot); survivors
-//    are inserted one at a time by a warp-wide shift (shuffles). After the
-//    tile, the CTA's warps merge their lists (warp g merges query g) and
-//    write the tile's top k to the workspace; a second kernel merges a
-//    query's tiles the same way and writes the sorted result.
+// Design (B200): score every candidate once at HBM speed, keep almost none.
+//  * Distances: a lane per candidate row, QG queries per CTA (their vectors
+//    or PQ tables in shared memory). L2 sums (q_d - r_d)^2 in float32 with
+//    packed f32x2 subtract/FMA from 16-byte row loads; PQ sums table entries
+//    in PqAdcDistance's order (four chains, (l0 + l1) + (l2 + l3), then the
+//    tail: bit-identical to the reference). A distance becomes a 32-bit key
+//    whose unsigned order is the float order, and (key, node) as one 64-bit
+//    value orders candidates as CloserFirst does (distance, then node id;
+//    engine/include/vectra/index/search_scratch.h:35-40).
+//  * Levels. Level 0 scores a spread sample (groups of 32 consecutive
+//    candidates, evenly spaced) and stores every key; a select kernel finds
+//    its k-th smallest key, an upper bound on the true k-th distance (at
+//    least k candidates are at or under it). Each further level scores a
+//    larger sample, or at last every candidate, and appends only the
+//    candidates at or under the current bound to a per-query buffer (a
+//    ballot and one atomic per warp); its select lowers the bound again.
+//    Sample sizes are planned so that the last level admits a few thousand
+//    candidates per query out of millions.
+//  * Select: one CTA of 1,024 threads per query holds the buffer's keys in
+//    registers and radix-selects the k-th (key, node) value with 11-bit
+//    digits (a shared-memory histogram per digit) until the entries at or
+//    under the current digit bucket fit a 2,048-entry bitonic sort; the
+//    sorted head is the result.
+//  * A last level that admits more candidates than its buffer holds (mass
+//    ties at the bound) is redone for that query by the warp-list scan:
+//    per-warp sorted lists in registers fed by ballot-filtered insertion,
+//    merged per tile and per query: exact for any input, slower.
 #include <math.h>
 #include <stdint.h>
 
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 #include <utility>
 #include <vector>
 
@@ -50,11 +50,587 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRowsPerLane = 16;
-constexpr int kTile = kThreads * kRowsPerLane;  // candidates per CTA tile
+constexpr int kMaxRowsPerLane = 16;
+constexpr int kListTile = kThreads * kMaxRowsPerLane;  // warp-list scan tile
 constexpr uint32_t kNoNode = 0xffffffffu;
+constexpr uint32_t kNoBound = 0xffffffffu;  // admits every key
 constexpr unsigned kFull = 0xffffffffu;
+// Candidate buffer per query (entries), and the select kernel's shape.
+constexpr int64_t kCap = 32768;
+constexpr int kSelThreads = 1024;
+constexpr int kSelKeys = int(kCap / kSelThreads);
+constexpr int kSortMax = 2048;
+// Candidates scored by level 0 when a query has more than kCap.
+constexpr int64_t kSample0 = 8192;
 
+// Unsigned order of the key = float order of the distance (-0 as +0, NaN
+// last).
+__device__ __forceinline__ uint32_t dist_key(float d) {
+  if (d != d) return 0xffffffffu;
+  uint32_t u = __float_as_uint(d);
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_dist(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
+}
+
+// Packed float pairs (sm_100a f32x2 arithmetic).
+__device__ __forceinline__ uint64_t pk(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ float2 upk(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Scorers: a CTA's queries in shared memory, and their distances to a row.
+// ---------------------------------------------------------------------------
+template <int QG>
+struct L2Score {
+  const float* queries;
+  int64_t query_stride;
+  const float* rows;
+  int64_t row_stride;
+  int dim;
+  int vec4;  // rows 16-byte aligned with dim % 4 == 0
+
+  static size_t smem_floats(int dim) { return size_t(QG) * ((dim + 3) & ~3); }
+  __device__ __forceinline__ int floats() const { return QG * ((dim + 3) & ~3); }
+
+  __device__ __forceinline__ void load(float* s, int64_t q0,
+                                       int64_t nq) const {
+    const int dpad = (dim + 3) & ~3;
+    for (int i = threadIdx.x; i < QG * dpad; i += blockDim.x) {
+      const int g = i / dpad, c = i - g * dpad;
+      s[i] = (q0 + g < nq && c < dim) ? queries[(q0 + g) * query_stride + c]
+                                      : 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void score(const float* sq, uint32_t node,
+                                        float (&dist)[QG]) const {
+    const int dpad = (dim + 3) & ~3;
+    const float* row = rows + int64_t(node) * row_stride;
+    uint64_t acc[QG][2];
+#pragma unroll
+    for (int g = 0; g < QG; ++g) acc[g][0] = acc[g][1] = 0;
+    if (vec4) {
+      // Eight 16-byte loads of the row in flight before any is used.
+      constexpr int kBatch = 8;
+      int c = 0;
+      for (; c + 4 * kBatch <= dim; c += 4 * kBatch) {
+        float4 rv[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b)
+          rv[b] = __ldg(reinterpret_cast<const float4*>(row + c + 4 * b));
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const uint64_t r01 = pk(rv[b].x, rv[b].y);
+          const uint64_t r23 = pk(rv[b].z, rv[b].w);
+#pragma unroll
+          for (int g = 0; g < QG; ++g) {
+            const float4 qv =
+                *reinterpret_cast<const float4*>(sq + g * dpad + c + 4 * b);
+            const uint64_t d01 = sub2(pk(qv.x, qv.y), r01);
+            const uint64_t d23 = sub2(pk(qv.z, qv.w), r23);
+            acc[g][0] = fma2(d01, d01, acc[g][0]);
+            acc[g][1] = fma2(d23, d23, acc[g][1]);
+          }
+        }
+      }
+      for (; c < dim; c += 4) {
+        const float4 rv = __ldg(reinterpret_cast<const float4*>(row + c));
+        const uint64_t r01 = pk(rv.x, rv.y), r23 = pk(rv.z, rv.w);
+#pragma unroll
+        for (int g = 0; g < QG; ++g) {
+          const float4 qv = *reinterpret_cast<const float4*>(sq + g * dpad + c);
+          const uint64_t d01 = sub2(pk(qv.x, qv.y), r01);
+          const uint64_t d23 = sub2(pk(qv.z, qv.w), r23);
+          acc[g][0] = fma2(d01, d01, acc[g][0]);
+          acc[g][1] = fma2(d23, d23, acc[g][1]);
+        }
+      }
+    } else {
+      // Element pairs (c, c + 1) in one packed accumulator; an odd last
+      // element in the other.
+      int c = 0;
+      for (; c + 2 <= dim; c += 2) {
+        const float r0 = __ldg(row + c), r1 = __ldg(row + c + 1);
+#pragma unroll
+        for (int g = 0; g < QG; ++g) {
+          const uint64_t dd =
+              pk(sq[g * dpad + c] - r0, sq[g * dpad + c + 1] - r1);
+          acc[g][0] = fma2(dd, dd, acc[g][0]);
+        }
+      }
+      if (c < dim) {
+        const float r0 = __ldg(row + c);
+#pragma unroll
+        for (int g = 0; g < QG; ++g) {
+          const uint64_t dd = pk(sq[g * dpad + c] - r0, 0.f);
+          acc[g][1] = fma2(dd, dd, acc[g][1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < QG; ++g) {
+      const float2 a = upk(acc[g][0]), b = upk(acc[g][1]);
+      dist[g] = (a.x + a.y) + (b.x + b.y);
+    }
+  }
+};
+
+// The sum of table entries for one code in PqAdcDistance's order
+// (simd_distance.cc:71-85): four chains, (l0 + l1) + (l2 + l3), then the
+// tail. Code bytes in a local array (any m).
+__device__ __forceinline__ float adc_sum_bytes(const float* t,
+                                               const uint8_t* code, int m) {
+  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+  int s = 0;
+  for (; s + 4 <= m; s += 4) {
+    l0 = __fadd_rn(l0, t[(s + 0) * 256 + code[s + 0]]);
+    l1 = __fadd_rn(l1, t[(s + 1) * 256 + code[s + 1]]);
+    l2 = __fadd_rn(l2, t[(s + 2) * 256 + code[s + 2]]);
+    l3 = __fadd_rn(l3, t[(s + 3) * 256 + code[s + 3]]);
+  }
+  float sum = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));
+  for (; s < m; ++s) sum = __fadd_rn(sum, t[s * 256 + code[s]]);
+  return sum;
+}
+
+// The same sum with MS known and the code bytes packed four to a 32-bit
+// word (registers).
+template <int MS>
+__device__ __forceinline__ float adc_sum_words(const float* t,
+                                               const uint32_t* w) {
+  auto at = [&](int s) {
+    return t[s * 256 + ((w[s >> 2] >> ((s & 3) * 8)) & 0xffu)];
+  };
+  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+  int s = 0;
+#pragma unroll
+  for (; s + 4 <= MS; s += 4) {
+    l0 = __fadd_rn(l0, at(s + 0));
+    l1 = __fadd_rn(l1, at(s + 1));
+    l2 = __fadd_rn(l2, at(s + 2));
+    l3 = __fadd_rn(l3, at(s + 3));
+  }
+  float sum = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));
+#pragma unroll
+  for (; s < MS; ++s) sum = __fadd_rn(sum, at(s));
+  return sum;
+}
+
+template <int QG, int MS>
+struct PqScore {
+  const float* tables;
+  const uint8_t* codes;
+  int64_t code_stride;
+  int m;
+
+  static size_t smem_floats(int m) {
+    return size_t(QG) * m * VECTRA_PQ_CENTROIDS;
+  }
+  __device__ __forceinline__ int floats() const {
+    return QG * m * VECTRA_PQ_CENTROIDS;
+  }
+
+  __device__ __forceinline__ void load(float* s, int64_t q0,
+                                       int64_t nq) const {
+    const int tsz = m * VECTRA_PQ_CENTROIDS;
+    for (int i = threadIdx.x; i < QG * tsz; i += blockDim.x) {
+      const int g = i / tsz;
+      s[i] = q0 + g < nq ? tables[(q0 + g) * tsz + (i - g * tsz)] : 0.f;
+    }
+  }
+
+  // MS > 0 kernels run only on codes whose address and stride are aligned
+  // to their 8- or 16-byte loads.
+  __device__ __forceinline__ void score(const float* st, uint32_t node,
+                                        float (&dist)[QG]) const {
+    const int tsz = m * VECTRA_PQ_CENTROIDS;
+    const uint8_t* cp = codes + int64_t(node) * code_stride;
+    if constexpr (MS >= 8) {
+      uint32_t w[MS / 4];
+      if constexpr (MS == 8) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(cp));
+        w[0] = v.x;
+        w[1] = v.y;
+      } else {
+#pragma unroll
+        for (int i = 0; i < MS / 16; ++i) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(cp) + i);
+          w[4 * i + 0] = v.x;
+          w[4 * i + 1] = v.y;
+          w[4 * i + 2] = v.z;
+          w[4 * i + 3] = v.w;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < QG; ++g) dist[g] = adc_sum_words<MS>(st + g * tsz, w);
+    } else {
+      uint8_t b[VECTRA_SCAN_MAX_SUBSPACES];
+      for (int s = 0; s < m; ++s) b[s] = __ldg(cp + s);
+#pragma unroll
+      for (int g = 0; g < QG; ++g) dist[g] = adc_sum_bytes(st + g * tsz, b, m);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Levels: score a sample (or every candidate), store or append keys.
+// ---------------------------------------------------------------------------
+struct Level {
+  int64_t n_queries;
+  int64_t n_rows;
+  const int64_t* offsets;  // per-query candidates (CSR), or null: every row
+  const uint32_t* ids;
+  int64_t groups;          // sampled groups of 32 candidates; 0: every one
+  int rows_per_lane;       // a CTA tile is 256 x rows_per_lane candidates
+  int64_t n_slots;         // CTAs per query group
+  const uint32_t* bound;   // admission keys; null: store every key (level 0)
+  uint32_t* keys;          // [n_queries][cap]
+  uint32_t* nodes;         // [n_queries][cap]
+  uint32_t* count;         // [n_queries] entries stored or offered
+  int64_t cap;
+};
+
+__device__ __forceinline__ int64_t cand_count(const Level& L, int64_t q) {
+  return L.offsets == nullptr ? L.n_rows : L.offsets[q + 1] - L.offsets[q];
+}
+
+// One launch per level. A group's queries share their candidates (per-query
+// candidate lists run with QG = 1). Scan index j of a query maps to its
+// candidate j (every candidate) or to (j / 32) * spacing + j % 32 (a sample
+// of groups of 32 consecutive candidates).
+template <int QG, class Score>
+__global__ void __launch_bounds__(kThreads)
+    level_kernel(Score sc, Level L) {
+  extern __shared__ __align__(16) float smem_f[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n_groups = (L.n_queries + QG - 1) / QG;
+  const int64_t group = blockIdx.x % n_groups;
+  const int64_t slot = blockIdx.x / n_groups;
+  const int64_t q0 = group * QG;
+  const int64_t n = cand_count(L, q0);
+  const bool every = L.groups == 0 || 32 * L.groups >= n;
+  const int64_t m = every ? n : 32 * L.groups;
+  const int64_t spacing = every ? 0 : n / L.groups;
+  const int64_t tile = int64_t(kThreads) * L.rows_per_lane;
+  const bool store_all = L.bound == nullptr;
+  // Level 0 stores scan index j at entry j: no more than the buffer holds
+  // (a query's list longer than the stated maximum is cut there).
+  if (store_all && slot == 0 && threadIdx.x < QG &&
+      q0 + threadIdx.x < L.n_queries)
+    L.count[q0 + threadIdx.x] = uint32_t(m < L.cap ? m : L.cap);
+  if (slot * tile >= m) return;
+  sc.load(smem_f, q0, L.n_queries);
+  __syncthreads();
+  uint32_t bound[QG];
+#pragma unroll
+  for (int g = 0; g < QG; ++g)
+    bound[g] = (!store_all && q0 + g < L.n_queries) ? L.bound[q0 + g]
+                                                    : kNoBound;
+  const int64_t id0 = L.offsets != nullptr ? L.offsets[q0] : 0;
+  for (int64_t t = slot; t * tile < m; t += L.n_slots) {
+    for (int r = 0; r < L.rows_per_lane; ++r) {
+      const int64_t j0 = t * tile + (int64_t(r) * kWarps + warp) * 32;
+      if (j0 >= m) break;  // warp-uniform
+      const int64_t j = j0 + lane;
+      const bool valid = j < m;
+      const int64_t i = every ? j : (j >> 5) * spacing + (j & 31);
+      const uint32_t node = !valid ? kNoNode
+                            : L.offsets != nullptr ? L.ids[id0 + i]
+                                                   : uint32_t(i);
+      float dist[QG];
+      if (valid) sc.score(smem_f, node, dist);
+#pragma unroll
+      for (int g = 0; g < QG; ++g) {
+        const int64_t q = q0 + g;
+        if (q >= L.n_queries) break;  // uniform
+        const uint32_t key = valid ? dist_key(dist[g]) : kNoBound;
+        uint32_t* qk = L.keys + q * L.cap;
+        uint32_t* qn = L.nodes + q * L.cap;
+        if (store_all) {
+          if (valid && j < L.cap) {
+            qk[j] = key;
+            qn[j] = node;
+          }
+          continue;
+        }
+        const bool admit = valid && key <= bound[g];
+        const unsigned bal = __ballot_sync(kFull, admit);
+        if (bal == 0u) continue;
+        const int leader = __ffs(bal) - 1;
+        uint32_t pos = 0;
+        if (lane == leader)
+          pos = atomicAdd(L.count + q, uint32_t(__popc(bal)));
+        pos = __shfl_sync(kFull, pos, leader) +
+              uint32_t(__popc(bal & ((1u << lane) - 1u)));
+        if (admit && pos < L.cap) {
+          qk[pos] = key;
+          qn[pos] = node;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Select: the k smallest (key, node) values of a query's buffer.
+// ---------------------------------------------------------------------------
+enum SelectMode { kFirstBound = 0, kLowerBound = 1, kFinal = 2 };
+
+struct Select {
+  int64_t cap;
+  int k;
+  int mode;
+  const uint32_t* keys;
+  const uint32_t* nodes;
+  uint32_t* count;     // read, then reset for the next level
+  uint32_t* bound;     // per-query admission key (bound modes)
+  float* out_d;        // final: results
+  uint32_t* out_n;
+  int32_t* counts;     // may be null
+  int32_t* overflow;   // final: 1 where the buffer overflowed
+  float* fb_d;         // final: the bound as a distance, for the re-scan
+  uint32_t* fb_n;
+};
+
+// Exclusive prefix sum over the block's 1,024 threads; *total gets the sum.
+__device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t* wtot,
+                                               uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(kFull, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wtot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = wtot[lane];
+    uint32_t s = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFull, s, o);
+      if (lane >= o) s += y;
+    }
+    wtot[lane] = s - w;
+    if (lane == 31) wtot[32] = s;
+  }
+  __syncthreads();
+  const uint32_t r = wtot[warp] + x - v;
+  *total = wtot[32];
+  __syncthreads();  // wtot may be reused
+  return r;
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
+  __shared__ uint32_t hist[2048];
+  __shared__ uint32_t wtot[33];
+  __shared__ uint32_t pick[3];
+  __shared__ unsigned long long sorted[kSortMax];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t q = blockIdx.x;
+  const uint32_t n_total = a.count[q];
+  const int64_t n = int64_t(n_total) < a.cap ? int64_t(n_total) : a.cap;
+  const uint32_t* qk = a.keys + q * a.cap;
+  const uint32_t* qn = a.nodes + q * a.cap;
+  uint32_t key[kSelKeys];
+#pragma unroll
+  for (int i = 0; i < kSelKeys; ++i) {
+    const int64_t idx = int64_t(i) * kSelThreads + tid;
+    key[i] = idx < n ? qk[idx] : kNoBound;
+  }
+  hist[tid] = 0u;
+  hist[tid + kSelThreads] = 0u;
+  __syncthreads();  // every thread has read the count
+  if (tid == 0) a.count[q] = 0u;  // the next level appends from zero
+  const uint32_t need = uint32_t(int64_t(a.k) < n ? int64_t(a.k) : n);
+  if (a.mode == kFinal) {
+    const bool over = n_total > a.cap;
+    if (tid == 0) {
+      // The re-scan's bound: this query's, or none admitted when it is not
+      // re-scanned (its CTAs may still run beside a query that is).
+      a.overflow[q] = over ? 1 : 0;
+      const uint32_t b = a.bound[q];
+      a.fb_d[q] = !over ? -INFINITY : b == kNoBound ? INFINITY : key_dist(b);
+      a.fb_n[q] = kNoNode;
+    }
+    if (over) return;  // the warp-list re-scan writes this query
+    if (need == 0u) {
+      for (int j = tid; j < a.k; j += kSelThreads) {
+        a.out_d[q * a.k + j] = INFINITY;
+        a.out_n[q * a.k + j] = kNoNode;
+      }
+      if (tid == 0 && a.counts != nullptr) a.counts[q] = 0;
+      return;
+    }
+  } else if (need < uint32_t(a.k)) {  // fewer than k: no bound from here
+    if (tid == 0 && a.mode == kFirstBound) a.bound[q] = kNoBound;
+    return;
+  }
+
+  // Radix select of the need-th smallest (key << 32 | node): 11/11/10-bit
+  // digits of the key, then of the node, until the entries at or under the
+  // bucket fit the sort buffer.
+  uint64_t pre = 0;      // the selected digits so far, in place
+  int pbits = 0;         // how many top bits they fix
+  uint32_t below = 0;    // entries under the bucket
+  uint32_t in_bucket = uint32_t(n);
+  for (int round = 0; round < 6 && below + in_bucket > uint32_t(kSortMax);
+       ++round) {
+    const int w = round % 3 == 2 ? 10 : 11;
+    const int shift = 64 - pbits - w;
+    const uint32_t pk32 = uint32_t(pre >> 32);
+#pragma unroll
+    for (int i = 0; i < kSelKeys; ++i) {
+      if (int64_t(i) * kSelThreads + warp * 32 >= n) break;  // warp-uniform
+      const int64_t idx = int64_t(i) * kSelThreads + tid;
+      bool inb = idx < n;
+      uint32_t bin = 0;
+      if (inb) {
+        if (pbits < 32) {
+          inb = pbits == 0 ||
+                (key[i] >> (32 - pbits)) == (pk32 >> (32 - pbits));
+          bin = (key[i] >> (shift - 32)) & ((1u << w) - 1u);
+        } else {
+          inb = key[i] == pk32;
+          if (inb) {
+            const uint32_t nd = qn[idx];
+            const int nb = pbits - 32;
+            inb = nb == 0 || (nd >> (32 - nb)) == (uint32_t(pre) >> (32 - nb));
+            bin = (nd >> shift) & ((1u << w) - 1u);
+          }
+        }
+      }
+      const unsigned act = __ballot_sync(kFull, inb);
+      if (inb) {
+        const unsigned peers = __match_any_sync(act, bin);
+        if (lane == __ffs(peers) - 1)
+          atomicAdd(&hist[bin], uint32_t(__popc(peers)));
+      }
+    }
+    __syncthreads();
+    const uint32_t h0 = hist[2 * tid], h1 = hist[2 * tid + 1];
+    uint32_t total;
+    const uint32_t ex = block_scan(h0 + h1, wtot, &total);
+    const uint32_t r = need - below;  // rank inside the bucket, from 1
+    if (ex < r && r <= ex + h0) {
+      pick[0] = 2 * tid;
+      pick[1] = ex;
+      pick[2] = h0;
+    } else if (ex + h0 < r && r <= ex + h0 + h1) {
+      pick[0] = 2 * tid + 1;
+      pick[1] = ex + h0;
+      pick[2] = h1;
+    }
+    hist[2 * tid] = 0u;
+    hist[2 * tid + 1] = 0u;
+    __syncthreads();
+    pre |= uint64_t(pick[0]) << shift;
+    pbits += w;
+    below += pick[1];
+    in_bucket = pick[2];
+    __syncthreads();  // pick is rewritten next round
+  }
+
+  // Gather the entries at or under the bucket (strictly under it when they
+  // are copies of one value beyond the buffer) and sort them.
+  const bool copies = below + in_bucket > uint32_t(kSortMax);
+  const uint32_t pk32 = uint32_t(pre >> 32), pn32 = uint32_t(pre);
+  uint32_t sel = 0u;
+#pragma unroll
+  for (int i = 0; i < kSelKeys; ++i) {
+    const int64_t idx = int64_t(i) * kSelThreads + tid;
+    if (idx >= n) break;
+    bool s;
+    if (pbits == 0) {
+      s = true;
+    } else if (pbits <= 32) {
+      s = (key[i] >> (32 - pbits)) <= (pk32 >> (32 - pbits));
+    } else if (key[i] != pk32) {
+      s = key[i] < pk32;
+    } else {
+      const uint32_t nd = qn[idx];
+      s = copies ? nd < pn32 : (nd >> (64 - pbits)) <= (pn32 >> (64 - pbits));
+    }
+    if (s) sel |= 1u << i;
+  }
+  uint32_t n_sel;
+  uint32_t off = block_scan(uint32_t(__popc(sel)), wtot, &n_sel);
+#pragma unroll
+  for (int i = 0; i < kSelKeys; ++i) {
+    if (sel & (1u << i)) {
+      if (off < uint32_t(kSortMax))
+        sorted[off] = (uint64_t(key[i]) << 32) |
+                      qn[int64_t(i) * kSelThreads + tid];
+      ++off;
+    }
+  }
+  n_sel = n_sel < uint32_t(kSortMax) ? n_sel : uint32_t(kSortMax);
+  uint32_t p2 = 2;
+  while (p2 < n_sel) p2 <<= 1;
+  for (uint32_t i = n_sel + tid; i < p2; i += kSelThreads) sorted[i] = ~0ull;
+  __syncthreads();
+  for (uint32_t size = 2; size <= p2; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = tid; i < p2 / 2; i += kSelThreads) {
+        const uint32_t lo = (i / stride) * 2 * stride + (i % stride);
+        const uint32_t hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const unsigned long long x = sorted[lo], y = sorted[hi];
+        if ((x > y) == up) {
+          sorted[lo] = y;
+          sorted[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (a.mode != kFinal) {
+    if (tid == 0) {
+      const uint32_t kth =
+          uint32_t((copies && need > below ? pre : sorted[need - 1]) >> 32);
+      a.bound[q] = a.mode == kFirstBound ? kth : umin(a.bound[q], kth);
+    }
+    return;
+  }
+  for (uint32_t j = tid; j < uint32_t(a.k); j += kSelThreads) {
+    float d = INFINITY;
+    uint32_t nd = kNoNode;
+    if (j < need) {
+      const uint64_t c = copies && j >= below ? pre : sorted[j];
+      d = key_dist(uint32_t(c >> 32));
+      nd = uint32_t(c);
+    }
+    a.out_d[q * a.k + j] = d;
+    a.out_n[q * a.k + j] = nd;
+  }
+  if (tid == 0 && a.counts != nullptr) a.counts[q] = int32_t(need);
+}
+
+// ---------------------------------------------------------------------------
+// The warp-list scan: exact for any input; re-does the queries whose last
+// level overflowed its buffer.
+// ---------------------------------------------------------------------------
 __device__ __forceinline__ bool closer(float da, uint32_t na, float db,
                                        uint32_t nb) {
   return da < db || (da == db && na < nb);
@@ -151,107 +727,21 @@ struct WarpList {
   }
 };
 
-// Packed float pairs (sm_100a f32x2 arithmetic).
-__device__ __forceinline__ uint64_t pk(float x, float y) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
-  return r;
-}
-__device__ __forceinline__ float2 upk(uint64_t v) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-
-struct ScanShape {
+struct ListShape {
   int64_t n_queries;
   int64_t n_rows;
-  int64_t n_tiles;        // tiles per query (of the largest candidate set)
-  int64_t scan_tiles;     // tiles this launch scans (n_tiles, or 1: sample)
-  int64_t n_slots;        // CTAs (and partial lists) per query group
+  int64_t n_tiles;         // tiles of the largest candidate set
+  int64_t n_slots;         // CTAs (and partial lists) per query group
   const int64_t* offsets;  // per-query candidates (CSR), or null
   const uint32_t* ids;
-  const float* bound_d;   // per-query admission bound, or null
+  const float* bound_d;    // per-query admission bound
   const uint32_t* bound_n;
-  float* sample_out;      // sample mode: per-query bound to lower, or null
+  const int32_t* only;     // queries to scan (nonzero), or null: all
   int k;
 };
 
-// Lowers *addr to v (atomically, float order).
-__device__ __forceinline__ void atomic_min_float(float* addr, float v) {
-  if (!(v == v)) return;  // NaN
-  unsigned int* a = reinterpret_cast<unsigned int*>(addr);
-  unsigned int old = *a, assumed;
-  do {
-    assumed = old;
-    if (__uint_as_float(assumed) <= v) return;
-    old = atomicCAS(a, assumed, __float_as_uint(v));
-  } while (old != assumed);
-}
-
-// Sample mode: each lane's minimum distance over its rows of the tile; the
-// k-th smallest of the CTA's 256 lane minima bounds the tile's k-th nearest
-// from above (at least k rows are at or under it), and the smallest such
-// bound over the sampled tiles bounds the scan's. `mins` are per query.
-template <int QG>
-__device__ __forceinline__ void sample_bound(const float (&mins)[QG],
-                                             float* sbuf, int64_t q0,
-                                             const ScanShape& sh) {
-  const int t = threadIdx.x;
-#pragma unroll
-  for (int g = 0; g < QG; ++g) sbuf[g * kThreads + t] = mins[g];
-  __syncthreads();
-  // Bitonic sort of each query's 256 minima, ascending.
-  for (int size = 2; size <= kThreads; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      const int partner = t ^ stride;
-      if (partner > t) {
-        const bool up = (t & size) == 0;
-#pragma unroll
-        for (int g = 0; g < QG; ++g) {
-          float& a = sbuf[g * kThreads + t];
-          float& b = sbuf[g * kThreads + partner];
-          if ((a > b) == up) {
-            const float x = a;
-            a = b;
-            b = x;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  if (t < QG && q0 + t < sh.n_queries)
-    atomic_min_float(sh.sample_out + q0 + t,
-                     sbuf[t * kThreads + (sh.k - 1 < kThreads ? sh.k - 1
-                                                                : kThreads - 1)]);
-}
-
-// The admission bound of query q: candidates farther than it are not
-// offered (+inf / no bound when absent).
-__device__ __forceinline__ void bound_of(const ScanShape& sh, int64_t q,
-                                         float& bd, uint32_t& bn) {
-  if (sh.bound_d != nullptr && q < sh.n_queries) {
-    bd = sh.bound_d[q];
-    bn = sh.bound_n[q];
-  } else {
-    bd = INFINITY;
-    bn = kNoNode;
-  }
-}
-
-// Candidate i of query q's tile-relative range: its node id, or kNoNode.
-__device__ __forceinline__ uint32_t candidate(const ScanShape& sh, int64_t q,
+// Candidate i of query q: its node id, or kNoNode.
+__device__ __forceinline__ uint32_t candidate(const ListShape& sh, int64_t q,
                                               int64_t i) {
   if (sh.offsets == nullptr) return i < sh.n_rows ? uint32_t(i) : kNoNode;
   const int64_t lo = sh.offsets[q], hi = sh.offsets[q + 1];
@@ -263,8 +753,8 @@ __device__ __forceinline__ uint32_t candidate(const ScanShape& sh, int64_t q,
 template <int KPW, int QG>
 __device__ __forceinline__ void merge_tile(WarpList<KPW> (&lists)[QG],
                                            float* sd, uint32_t* sn,
-                                           int64_t q0, int64_t nq, int64_t slot,
-                                           const ScanShape& sh, float* wd,
+                                           int64_t q0, int64_t slot,
+                                           const ListShape& sh, float* wd,
                                            uint32_t* wn) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k = sh.k;
@@ -279,7 +769,7 @@ __device__ __forceinline__ void merge_tile(WarpList<KPW> (&lists)[QG],
     }
   __syncthreads();
   for (int g = warp; g < QG; g += kWarps) {
-    if (q0 + g >= nq) continue;
+    if (q0 + g >= sh.n_queries) continue;
     WarpList<KPW> m;
 #pragma unroll
     for (int s = 0; s < KPW; ++s) {
@@ -299,248 +789,75 @@ __device__ __forceinline__ void merge_tile(WarpList<KPW> (&lists)[QG],
   }
 }
 
-// ---------------------------------------------------------------------------
-// L2 scan.
-// ---------------------------------------------------------------------------
-template <int KPW, int QG>
+template <int KPW, int QG, class Score>
 __global__ void __launch_bounds__(kThreads)
-    l2_scan_kernel(const float* __restrict__ queries, int64_t query_stride,
-                   const float* __restrict__ rows, int64_t row_stride,
-                   int dim, int vec4, float* wd, uint32_t* wn, ScanShape sh) {
+    list_scan_kernel(Score sc, float* wd, uint32_t* wn, ListShape sh) {
   extern __shared__ __align__(16) float smem_f[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_groups = (sh.n_queries + QG - 1) / QG;
   const int64_t group = blockIdx.x % n_groups;
   const int64_t slot = blockIdx.x / n_groups;
   const int64_t q0 = group * QG;
-  const int dpad = (dim + 3) & ~3;
-  float* sq = smem_f;                         // [QG][dpad]
-  float* sd = sq + QG * dpad;                 // merge area
-  uint32_t* sn = reinterpret_cast<uint32_t*>(sd + QG * kWarps * KPW * 32);
-  for (int i = threadIdx.x; i < QG * dpad; i += kThreads) {
-    const int g = i / dpad, c = i - g * dpad;
-    sq[i] = (q0 + g < sh.n_queries && c < dim)
-                ? queries[(q0 + g) * query_stride + c]
-                : 0.f;
+  if (sh.only != nullptr) {
+    bool any = false;
+#pragma unroll
+    for (int g = 0; g < QG; ++g)
+      any |= q0 + g < sh.n_queries && sh.only[q0 + g] != 0;
+    if (!any) return;
   }
+  float* sq = smem_f;
+  sc.load(sq, q0, sh.n_queries);
   __syncthreads();
+  // The merge area follows the queries' floats.
+  float* sd = smem_f + sc.floats();
+  uint32_t* sn = reinterpret_cast<uint32_t*>(sd + QG * kWarps * KPW * 32);
 
   WarpList<KPW> lists[QG];
   float bd[QG];
   uint32_t bn[QG];
-  float mins[QG];
-  const bool sampling = sh.sample_out != nullptr;
 #pragma unroll
   for (int g = 0; g < QG; ++g) {
     lists[g].clear();
-    bound_of(sh, q0 + g, bd[g], bn[g]);
-    mins[g] = INFINITY;
+    const int64_t q = q0 + g;
+    bd[g] = q < sh.n_queries ? sh.bound_d[q] : INFINITY;
+    bn[g] = q < sh.n_queries ? sh.bound_n[q] : kNoNode;
   }
-  for (int64_t tile = slot; tile < sh.scan_tiles; tile += sh.n_slots)
-  for (int r = 0; r < kRowsPerLane; ++r) {
-    const int64_t i = tile * kTile + (int64_t(r) * kWarps + warp) * 32 + lane;
-    // Candidates of a group's queries coincide (per-query lists use QG = 1).
-    const uint32_t node = candidate(sh, q0, i);
-    float dist[QG];
-    if (node != kNoNode) {
-      const float* row = rows + int64_t(node) * row_stride;
-      uint64_t acc[QG][2];
-#pragma unroll
-      for (int g = 0; g < QG; ++g) acc[g][0] = acc[g][1] = 0;
-      if (vec4) {
-        // Eight 16-byte loads of the row in flight before any is used.
-        constexpr int kBatch = 8;
-        int c = 0;
-        for (; c + 4 * kBatch <= dim; c += 4 * kBatch) {
-          float4 rv[kBatch];
-#pragma unroll
-          for (int b = 0; b < kBatch; ++b)
-            rv[b] = __ldg(reinterpret_cast<const float4*>(row + c + 4 * b));
-#pragma unroll
-          for (int b = 0; b < kBatch; ++b) {
-            const uint64_t r01 = pk(rv[b].x, rv[b].y);
-            const uint64_t r23 = pk(rv[b].z, rv[b].w);
-#pragma unroll
-            for (int g = 0; g < QG; ++g) {
-              const float4 qv = *reinterpret_cast<const float4*>(
-                  sq + g * dpad + c + 4 * b);
-              const uint64_t d01 = sub2(pk(qv.x, qv.y), r01);
-              const uint64_t d23 = sub2(pk(qv.z, qv.w), r23);
-              acc[g][0] = fma2(d01, d01, acc[g][0]);
-              acc[g][1] = fma2(d23, d23, acc[g][1]);
-            }
-          }
-        }
-        for (; c < dim; c += 4) {
-          const float4 rv = __ldg(reinterpret_cast<const float4*>(row + c));
-          const uint64_t r01 = pk(rv.x, rv.y), r23 = pk(rv.z, rv.w);
-#pragma unroll
-          for (int g = 0; g < QG; ++g) {
-            const float4 qv = *reinterpret_cast<const float4*>(sq + g * dpad + c);
-            const uint64_t d01 = sub2(pk(qv.x, qv.y), r01);
-            const uint64_t d23 = sub2(pk(qv.z, qv.w), r23);
-            acc[g][0] = fma2(d01, d01, acc[g][0]);
-            acc[g][1] = fma2(d23, d23, acc[g][1]);
-          }
-        }
+  for (int64_t tile = slot; tile < sh.n_tiles; tile += sh.n_slots)
+    for (int r = 0; r < kMaxRowsPerLane; ++r) {
+      const int64_t i =
+          tile * kListTile + (int64_t(r) * kWarps + warp) * 32 + lane;
+      // Candidates of a group's queries coincide (per-query lists use
+      // QG = 1).
+      const uint32_t node = candidate(sh, q0, i);
+      float dist[QG];
+      if (node != kNoNode) {
+        sc.score(sq, node, dist);
       } else {
-        for (int c = 0; c < dim; ++c) {
-          const float rv = __ldg(row + c);
 #pragma unroll
-          for (int g = 0; g < QG; ++g) {
-            const uint64_t dd = pk(sq[g * dpad + c] - rv, 0.f);
-            acc[g][c & 1] = fma2(dd, dd, acc[g][c & 1]);
-          }
-        }
+        for (int g = 0; g < QG; ++g) dist[g] = INFINITY;
       }
 #pragma unroll
       for (int g = 0; g < QG; ++g) {
-        const float2 a = upk(acc[g][0]), b = upk(acc[g][1]);
-        dist[g] = (a.x + a.y) + (b.x + b.y);
+        const bool admit = !closer(bd[g], bn[g], dist[g], node);
+        lists[g].offer(admit ? dist[g] : INFINITY, admit ? node : kNoNode,
+                       sh.k, lane);
       }
-    } else {
-#pragma unroll
-      for (int g = 0; g < QG; ++g) dist[g] = INFINITY;
     }
-    if (sampling) {
-#pragma unroll
-      for (int g = 0; g < QG; ++g) mins[g] = fminf(mins[g], dist[g]);
-      continue;
-    }
-#pragma unroll
-    for (int g = 0; g < QG; ++g) {
-      const bool admit = !closer(bd[g], bn[g], dist[g], node);
-      lists[g].offer(admit ? dist[g] : INFINITY, admit ? node : kNoNode,
-                     sh.k, lane);
-    }
-  }
-  if (sampling) {
-    sample_bound<QG>(mins, sd, q0, sh);
-    return;
-  }
-  merge_tile<KPW, QG>(lists, sd, sn, q0, sh.n_queries, slot, sh, wd, wn);
+  merge_tile<KPW, QG>(lists, sd, sn, q0, slot, sh, wd, wn);
 }
 
-// ---------------------------------------------------------------------------
-// PQ (asymmetric distance) scan.
-// ---------------------------------------------------------------------------
-// The sum of table entries for one code in PqAdcDistance's order; MS > 0:
-// MS sub-spaces known at compile time (code bytes in registers).
-template <int MS>
-__device__ __forceinline__ float adc_sum(const float* t, const uint8_t* code,
-                                         int m) {
-  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-  const int mm = MS > 0 ? MS : m;
-  int s = 0;
-#pragma unroll
-  for (; s + 4 <= mm; s += 4) {
-    l0 = __fadd_rn(l0, t[(s + 0) * 256 + code[s + 0]]);
-    l1 = __fadd_rn(l1, t[(s + 1) * 256 + code[s + 1]]);
-    l2 = __fadd_rn(l2, t[(s + 2) * 256 + code[s + 2]]);
-    l3 = __fadd_rn(l3, t[(s + 3) * 256 + code[s + 3]]);
-  }
-  float sum = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));
-#pragma unroll
-  for (; s < mm; ++s) sum = __fadd_rn(sum, t[s * 256 + code[s]]);
-  return sum;
-}
-
-template <int KPW, int QG, int MS>
-__global__ void __launch_bounds__(kThreads)
-    pq_scan_kernel(const float* __restrict__ tables,
-                   const uint8_t* __restrict__ codes, int64_t code_stride,
-                   int m, int vec16, float* wd, uint32_t* wn, ScanShape sh) {
-  extern __shared__ __align__(16) float smem_f[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n_groups = (sh.n_queries + QG - 1) / QG;
-  const int64_t group = blockIdx.x % n_groups;
-  const int64_t slot = blockIdx.x / n_groups;
-  const int64_t q0 = group * QG;
-  const int tsz = m * VECTRA_PQ_CENTROIDS;
-  float* st = smem_f;                          // [QG][m][256]
-  float* sd = st + QG * tsz;
-  uint32_t* sn = reinterpret_cast<uint32_t*>(sd + QG * kWarps * KPW * 32);
-  for (int i = threadIdx.x; i < QG * tsz; i += kThreads) {
-    const int g = i / tsz;
-    st[i] = q0 + g < sh.n_queries ? tables[(q0 + g) * tsz + (i - g * tsz)]
-                                  : 0.f;
-  }
-  __syncthreads();
-
-  WarpList<KPW> lists[QG];
-  float bd[QG];
-  uint32_t bn[QG];
-  float mins[QG];
-  const bool sampling = sh.sample_out != nullptr;
-#pragma unroll
-  for (int g = 0; g < QG; ++g) {
-    lists[g].clear();
-    bound_of(sh, q0 + g, bd[g], bn[g]);
-    mins[g] = INFINITY;
-  }
-  constexpr int kCodeBytes = MS > 0 ? MS : VECTRA_SCAN_MAX_SUBSPACES;
-  for (int64_t tile = slot; tile < sh.scan_tiles; tile += sh.n_slots)
-  for (int r = 0; r < kRowsPerLane; ++r) {
-    const int64_t i = tile * kTile + (int64_t(r) * kWarps + warp) * 32 + lane;
-    const uint32_t node = candidate(sh, q0, i);
-    float dist[QG];
-    if (node != kNoNode) {
-      const uint8_t* cp = codes + int64_t(node) * code_stride;
-      // The code: in registers when MS is known (16-byte loads), else in a
-      // local array.
-      union {
-        uint4 w[(kCodeBytes + 15) / 16];
-        uint8_t b[((kCodeBytes + 15) / 16) * 16];
-      } code;
-      if (MS > 0 && vec16) {
-#pragma unroll
-        for (int i = 0; i < (kCodeBytes + 15) / 16; ++i)
-          code.w[i] = __ldg(reinterpret_cast<const uint4*>(cp) + i);
-      } else {
-        for (int s = 0; s < m; ++s) code.b[s] = __ldg(cp + s);
-      }
-#pragma unroll
-      for (int g = 0; g < QG; ++g)
-        // PqAdcDistance (simd_distance.cc:71-85): four chains, then the
-        // tail, in this order.
-        dist[g] = adc_sum<MS>(st + g * tsz, code.b, m);
-    } else {
-#pragma unroll
-      for (int g = 0; g < QG; ++g) dist[g] = INFINITY;
-    }
-    if (sampling) {
-#pragma unroll
-      for (int g = 0; g < QG; ++g) mins[g] = fminf(mins[g], dist[g]);
-      continue;
-    }
-#pragma unroll
-    for (int g = 0; g < QG; ++g) {
-      const bool admit = !closer(bd[g], bn[g], dist[g], node);
-      lists[g].offer(admit ? dist[g] : INFINITY, admit ? node : kNoNode,
-                     sh.k, lane);
-    }
-  }
-  if (sampling) {
-    sample_bound<QG>(mins, sd, q0, sh);
-    return;
-  }
-  merge_tile<KPW, QG>(lists, sd, sn, q0, sh.n_queries, slot, sh, wd, wn);
-}
-
-// ---------------------------------------------------------------------------
-// Merge of a query's tiles: one warp per query.
-// ---------------------------------------------------------------------------
+// Merge of a query's partial lists: one CTA per query; warp w merges slots
+// w, w + 8, ... (the next batch's loads issued before the current batch is
+// offered); warp 0 merges the eight lists.
 template <int KPW>
 __global__ void __launch_bounds__(kThreads)
-    merge_kernel(const float* wd, const uint32_t* wn, ScanShape sh,
+    merge_kernel(const float* wd, const uint32_t* wn, ListShape sh,
                  float* out_d, uint32_t* out_n, int32_t* counts) {
-  // One CTA per query: warp w merges slots w, w + 8, ... (the next batch's
-  // loads issued before the current batch is offered); warp 0 merges the
-  // eight lists.
   __shared__ float md[kWarps * KPW * 32];
   __shared__ uint32_t mn[kWarps * KPW * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t q = blockIdx.x;
+  if (sh.only != nullptr && sh.only[q] == 0) return;
   constexpr int KP = KPW * 32;
   const int k = sh.k;
   const size_t base = size_t(q) * sh.n_slots * KP;
@@ -574,7 +891,8 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
   if (warp != 0) return;
-  for (int i = KP; i < kWarps * KP; i += 32) m.offer(md[i + lane], mn[i + lane], k, lane);
+  for (int i = KP; i < kWarps * KP; i += 32)
+    m.offer(md[i + lane], mn[i + lane], k, lane);
 #pragma unroll
   for (int s = 0; s < KPW; ++s) {
     const int j = s * 32 + lane;
@@ -584,21 +902,11 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   if (counts != nullptr) {
-    int64_t nc = sh.offsets == nullptr ? sh.n_rows
-                                       : sh.offsets[q + 1] - sh.offsets[q];
+    const int64_t nc = sh.offsets == nullptr
+                           ? sh.n_rows
+                           : sh.offsets[q + 1] - sh.offsets[q];
     if (lane == 0) counts[q] = int32_t(nc < k ? nc : k);
   }
-}
-
-// Admission bounds start open: (+inf, no node); the sample pass lowers the
-// distances, and the node stays kNoNode (every distance at or under the
-// bound is admitted).
-__global__ void bound_init_kernel(int64_t nq, float* bound_d,
-                                  uint32_t* bound_n) {
-  const int64_t q = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (q >= nq) return;
-  bound_d[q] = INFINITY;
-  bound_n[q] = kNoNode;
 }
 
 // ---------------------------------------------------------------------------
@@ -647,230 +955,356 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------
 int kpw_for(int k) { return k <= 32 ? 1 : k <= 64 ? 2 : k <= 128 ? 4 : 8; }
 
-// Partial lists per query group at most (the main pass's CTAs per group).
+// Partial lists per query group at most (the warp-list scan's CTAs).
 constexpr int64_t kMaxSlots = 512;
-// Tiles the sample pass bounds the scan from.
-constexpr int64_t kSampleTiles = 16;
 
-int64_t tiles_for(int64_t n_cand) {
-  return n_cand > 0 ? (n_cand + kTile - 1) / kTile : 1;
+int64_t list_tiles(int64_t n_cand) {
+  return n_cand > 0 ? (n_cand + kListTile - 1) / kListTile : 1;
 }
 
-// Workspace: partial lists [n_queries][slots][32 KPW] of distances, then of
-// nodes, then the admission bounds (distances, nodes) [n_queries].
-size_t workspace_for(int64_t n_queries, int64_t n_cand, int k) {
-  const int64_t slots = std::min(tiles_for(n_cand), kMaxSlots);
-  const size_t kp = size_t(kpw_for(k)) * 32;
-  const size_t lists = size_t(n_queries) * size_t(slots) * kp;
-  return ((lists * 4 + 15) & ~size_t(15)) * 2 + size_t(n_queries) * 8 + 256;
-}
-
-struct Workspace {
-  float* wd;
-  uint32_t* wn;
-  float* bound_d;
-  uint32_t* bound_n;
+// The levels of a scan of up to n_cand candidates per query: groups of 32
+// sampled per level (0 = every candidate; the last level is always that).
+struct Plan {
+  int n_levels = 0;
+  int64_t groups[8] = {};
+  int64_t cap = 0;        // buffer entries per query
+  bool rescan = false;    // the last level can overflow (warp-list re-scan)
 };
 
-// Sets a kernel's dynamic shared-memory limit once per (kernel, device).
-// (Instantiations that differ only in template values share a function
-// pointer type, so the record is kept by address.)
-cudaError_t allow_smem(const void* kern) {
+Plan plan_for(int64_t n_cand, int k) {
+  Plan p;
+  if (n_cand <= kCap) {  // one level stores every candidate
+    p.cap = std::max<int64_t>(n_cand, 1);
+    p.groups[p.n_levels++] = 0;
+    return p;
+  }
+  p.cap = kCap;
+  p.rescan = true;
+  int64_t s = kSample0;
+  p.groups[p.n_levels++] = s / 32;
+  // A level's bound is about the (k / s) quantile: the next level admits
+  // about k * (its size) / s candidates. Go to every candidate once that is
+  // at most a quarter of the buffer, else sample enough for an eighth.
+  while (p.n_levels < 6 && int64_t(k) * n_cand > (kCap / 4) * s) {
+    const int64_t s2 = s * (kCap / 8) / k;
+    if (2 * s2 >= n_cand) break;
+    p.groups[p.n_levels++] = s2 / 32;
+    s = s2;
+  }
+  p.groups[p.n_levels++] = 0;
+  return p;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace: keys and nodes [n_queries][cap], then count, bound, overflow,
+// re-scan bound (distance, node) [n_queries], then (plans that can overflow)
+// the warp-list scan's partial lists [n_queries][slots][32 KPW] of
+// distances and of nodes. Every part is written by a call before it reads
+// it; nothing needs clearing between calls.
+struct Workspace {
+  uint32_t* keys;
+  uint32_t* nodes;
+  uint32_t* count;
+  uint32_t* bound;
+  int32_t* overflow;
+  float* fb_d;
+  uint32_t* fb_n;
+  float* wd;
+  uint32_t* wn;
+};
+
+size_t list_bytes(int64_t n_queries, int64_t n_cand, int k) {
+  const int64_t slots = std::min(list_tiles(n_cand), kMaxSlots);
+  return align256(size_t(n_queries) * size_t(slots) * size_t(kpw_for(k)) *
+                  32 * 4);
+}
+
+size_t workspace_for(int64_t n_queries, int64_t n_cand, int k) {
+  const Plan p = plan_for(n_cand, k);
+  const size_t q = size_t(n_queries);
+  size_t bytes = 2 * align256(q * size_t(p.cap) * 4) + 5 * align256(q * 4);
+  if (p.rescan) bytes += 2 * list_bytes(n_queries, n_cand, k);
+  return bytes + 256;
+}
+
+Workspace carve(void* base_ptr, int64_t n_queries, int64_t n_cand, int k) {
+  const Plan p = plan_for(n_cand, k);
+  const size_t q = size_t(n_queries);
+  char* b = reinterpret_cast<char*>(
+      (reinterpret_cast<uintptr_t>(base_ptr) + 255) & ~uintptr_t(255));
+  Workspace w;
+  const size_t buf = align256(q * size_t(p.cap) * 4), small = align256(q * 4);
+  w.keys = reinterpret_cast<uint32_t*>(b);
+  w.nodes = reinterpret_cast<uint32_t*>(b + buf);
+  b += 2 * buf;
+  w.count = reinterpret_cast<uint32_t*>(b);
+  w.bound = reinterpret_cast<uint32_t*>(b + small);
+  w.overflow = reinterpret_cast<int32_t*>(b + 2 * small);
+  w.fb_d = reinterpret_cast<float*>(b + 3 * small);
+  w.fb_n = reinterpret_cast<uint32_t*>(b + 4 * small);
+  b += 5 * small;
+  w.wd = nullptr;
+  w.wn = nullptr;
+  if (p.rescan) {
+    const size_t lb = list_bytes(n_queries, n_cand, k);
+    w.wd = reinterpret_cast<float*>(b);
+    w.wn = reinterpret_cast<uint32_t*>(b + lb);
+  }
+  return w;
+}
+
+// Sets a kernel's dynamic shared-memory limit once per (kernel, device) and
+// returns how many of its CTAs fit an SM with `smem` bytes. (Instantiations
+// that differ only in template values share a function pointer type, so the
+// record is kept by address.)
+struct KernelRecord {
+  const void* kern;
+  int dev;
+  size_t smem;
+  int blocks;
+};
+
+cudaError_t prepare_kernel(const void* kern, size_t smem, int threads,
+                           int* blocks_per_sm) {
   static std::mutex mu;
-  static std::vector<std::pair<const void*, int>> done;
+  static std::vector<KernelRecord> done;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
-  for (const auto& e : done)
-    if (e.first == kern && e.second == dev) return cudaSuccess;
-  cudaError_t err = cudaFuncSetAttribute(
-      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  if (err == cudaSuccess) done.emplace_back(kern, dev);
-  return err;
-}
-
-template <int KPW, int QG, typename Kernel, typename... Args>
-cudaError_t launch_scan(Kernel kern, const ScanShape& sh, size_t smem,
-                        cudaStream_t stream, Args... args) {
-  cudaError_t err = allow_smem(reinterpret_cast<const void*>(kern));
-  if (err != cudaSuccess) return err;
-  const int64_t groups = (sh.n_queries + QG - 1) / QG;
-  const int64_t blocks = groups * sh.n_slots;
-  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  kern<<<dim3(unsigned(blocks)), kThreads, smem, stream>>>(args..., sh);
-  return cudaGetLastError();
-}
-
-template <int KPW>
-cudaError_t merge(const Workspace& w, const ScanShape& sh,
-                  const vectra_scan_results& res, cudaStream_t stream) {
-  merge_kernel<KPW><<<dim3(unsigned(sh.n_queries)), kThreads, 0, stream>>>(
-      w.wd, w.wn, sh, res.distances, res.nodes, res.counts);
-  return cudaGetLastError();
-}
-
-// The scan in four launches when the candidates span several tiles: the
-// sample pass over each query's first tile (one slot), its admission
-// bounds, the main pass with them, and the merge of the main pass's lists.
-template <int KPW, int QG, typename Launch>
-cudaError_t scan_passes(const ScanShape& base, const Workspace& w,
-                        const vectra_scan_results& res, cudaStream_t stream,
-                        Launch launch) {
-  ScanShape sh = base;
-  sh.bound_d = nullptr;
-  sh.bound_n = nullptr;
-  sh.sample_out = nullptr;
-  if (base.n_tiles > 1) {
-    // Bounds from the first kSampleTiles tiles, one CTA each.
-    const int64_t nb = (sh.n_queries + 127) / 128;
-    bound_init_kernel<<<dim3(unsigned(nb)), 128, 0, stream>>>(
-        sh.n_queries, w.bound_d, w.bound_n);
-    cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    sh.scan_tiles = std::min(base.n_tiles, kSampleTiles);
-    sh.n_slots = sh.scan_tiles;
-    sh.sample_out = w.bound_d;
-    if ((err = launch(sh)) != cudaSuccess) return err;
-    sh.sample_out = nullptr;
-    sh.bound_d = w.bound_d;
-    sh.bound_n = w.bound_n;
+  bool attr = false;
+  for (const auto& e : done) {
+    if (e.kern == kern && e.dev == dev) {
+      attr = true;
+      if (e.smem == smem) {
+        *blocks_per_sm = e.blocks;
+        return cudaSuccess;
+      }
+    }
   }
-  const int64_t groups = (sh.n_queries + QG - 1) / QG;
-  int64_t slots = (2 * int64_t(device_sm_count()) + groups - 1) / groups;
-  slots = std::max<int64_t>(1, std::min({slots, base.n_tiles, kMaxSlots}));
-  sh.scan_tiles = base.n_tiles;
-  sh.n_slots = slots;
-  cudaError_t err = launch(sh);
+  cudaError_t err = cudaSuccess;
+  if (!attr)
+    err = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (err != cudaSuccess) return err;
-  return merge<KPW>(w, sh, res, stream);
+  int blocks = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, threads,
+                                                      smem);
+  if (err != cudaSuccess) return err;
+  blocks = std::max(blocks, 1);
+  done.push_back({kern, dev, smem, blocks});
+  *blocks_per_sm = blocks;
+  return cudaSuccess;
 }
 
-template <int KPW, int QG>
-cudaError_t run_l2(const vectra_scan_l2_args* a, const ScanShape& sh,
-                   const Workspace& w, cudaStream_t stream) {
-  const int dpad = (a->dimension + 3) & ~3;
-  const size_t smem = size_t(QG) * dpad * 4 + size_t(QG) * kWarps * KPW * 32 * 8;
-  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  const int vec4 = (a->dimension % 4 == 0) && (a->row_stride % 4 == 0) &&
-                   (reinterpret_cast<uintptr_t>(a->rows) % 16 == 0);
-  return scan_passes<KPW, QG>(sh, w, a->results, stream,
-                              [&](const ScanShape& s2) {
-    return launch_scan<KPW, QG>(l2_scan_kernel<KPW, QG>, s2, smem, stream,
-                                a->queries, a->query_stride, a->rows,
-                                a->row_stride, a->dimension, vec4, w.wd,
-                                w.wn);
-  });
-}
+struct Common {
+  int64_t n_queries;
+  int64_t n_rows;
+  int64_t n_cand;  // the largest candidate set
+  vectra_scan_candidates cand;
+  vectra_scan_results res;
+  int k;
+};
 
-template <int KPW, int QG>
-cudaError_t run_pq(const vectra_scan_pq_args* a, const ScanShape& sh,
-                   const Workspace& w, cudaStream_t stream) {
-  const size_t smem = size_t(QG) * a->subspaces * VECTRA_PQ_CENTROIDS * 4 +
-                      size_t(QG) * kWarps * KPW * 32 * 8;
-  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  const int vec16 = (a->subspaces % 16 == 0) && (a->code_stride % 16 == 0) &&
-                    (reinterpret_cast<uintptr_t>(a->codes) % 16 == 0);
-  auto kernel = a->subspaces == 16 && vec16   ? pq_scan_kernel<KPW, QG, 16>
-                : a->subspaces == 8 && a->code_stride % 16 == 0 &&
-                          reinterpret_cast<uintptr_t>(a->codes) % 16 == 0
-                    ? pq_scan_kernel<KPW, QG, 8>
-                : a->subspaces == 32 && vec16 ? pq_scan_kernel<KPW, QG, 32>
-                : a->subspaces == 64 && vec16 ? pq_scan_kernel<KPW, QG, 64>
-                                              : pq_scan_kernel<KPW, QG, 0>;
-  const int vec_ok = a->subspaces == 8 ? (a->code_stride % 16 == 0 &&
-                                          reinterpret_cast<uintptr_t>(
-                                              a->codes) % 16 == 0)
-                                       : vec16;
-  return scan_passes<KPW, QG>(sh, w, a->results, stream,
-                              [&](const ScanShape& s2) {
-    return launch_scan<KPW, QG>(kernel, s2, smem, stream, a->tables, a->codes,
-                                a->code_stride, a->subspaces, vec_ok, w.wd,
-                                w.wn);
-  });
-}
-
-// Queries per CTA: 8 (or the most that fit beside the per-warp lists) for
-// scans of every row; 1 for per-query candidate lists.
-template <typename Run>
-cudaError_t by_kpw(int k, bool shared_candidates, int per_query_floats,
-                   Run run) {
-  const int kpw = kpw_for(k);
-  auto fits = [&](int qg) {
-    return size_t(qg) * per_query_floats * 4 + size_t(qg) * kWarps * kpw * 32 * 8 <=
-           size_t(200) * 1024;
+// The levels and selects of one scan, then the warp-list re-scan of the
+// queries whose last level overflowed (its CTAs return at once otherwise).
+template <int QG, class Score>
+cudaError_t run_levels(const Score& sc, size_t smem_floats, const Common& c,
+                       const Workspace& w, cudaStream_t stream) {
+  const Plan p = plan_for(c.n_cand, c.k);
+  const size_t smem = smem_floats * 4;
+  int per_sm = 1;
+  cudaError_t err = prepare_kernel(
+      reinterpret_cast<const void*>(level_kernel<QG, Score>), smem, kThreads,
+      &per_sm);
+  if (err != cudaSuccess) return err;
+  const int64_t n_groups = (c.n_queries + QG - 1) / QG;
+  const int64_t target = std::max<int64_t>(
+      1, (int64_t(per_sm) * device_sm_count() + n_groups - 1) / n_groups);
+  for (int l = 0; l < p.n_levels; ++l) {
+    Level L;
+    L.n_queries = c.n_queries;
+    L.n_rows = c.n_rows;
+    L.offsets = c.cand.offsets;
+    L.ids = c.cand.ids;
+    L.groups = p.groups[l];
+    const int64_t m = (L.groups == 0 || 32 * L.groups >= c.n_cand)
+                          ? c.n_cand
+                          : 32 * L.groups;
+    const int64_t tiles1 =
+        std::max<int64_t>(1, (m + kThreads - 1) / kThreads);
+    L.rows_per_lane = int(std::min<int64_t>(
+        kMaxRowsPerLane,
+        std::max<int64_t>(1, (tiles1 + target - 1) / target)));
+    const int64_t tile = int64_t(kThreads) * L.rows_per_lane;
+    L.n_slots = std::max<int64_t>(1, std::min(target, (m + tile - 1) / tile));
+    L.bound = l == 0 ? nullptr : w.bound;
+    L.keys = w.keys;
+    L.nodes = w.nodes;
+    L.count = w.count;
+    L.cap = p.cap;
+    const int64_t blocks = n_groups * L.n_slots;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+    level_kernel<QG, Score>
+        <<<dim3(unsigned(blocks)), kThreads, smem, stream>>>(sc, L);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    Select s;
+    s.cap = p.cap;
+    s.k = c.k;
+    s.mode = l + 1 == p.n_levels ? kFinal : l == 0 ? kFirstBound : kLowerBound;
+    s.keys = w.keys;
+    s.nodes = w.nodes;
+    s.count = w.count;
+    s.bound = w.bound;
+    s.out_d = c.res.distances;
+    s.out_n = c.res.nodes;
+    s.counts = c.res.counts;
+    s.overflow = w.overflow;
+    s.fb_d = w.fb_d;
+    s.fb_n = w.fb_n;
+    select_kernel<<<dim3(unsigned(c.n_queries)), kSelThreads, 0, stream>>>(s);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  if (!p.rescan) return cudaSuccess;
+  // The warp-list re-scan.
+  auto go = [&](auto kpw_tag) -> cudaError_t {
+    constexpr int KPW = decltype(kpw_tag)::value;
+    const size_t lsmem = smem + size_t(QG) * kWarps * KPW * 32 * 8;
+    if (lsmem > 227 * 1024) return cudaErrorInvalidConfiguration;
+    int lper = 1;
+    cudaError_t e = prepare_kernel(
+        reinterpret_cast<const void*>(list_scan_kernel<KPW, QG, Score>),
+        lsmem, kThreads, &lper);
+    if (e != cudaSuccess) return e;
+    ListShape sh;
+    sh.n_queries = c.n_queries;
+    sh.n_rows = c.n_rows;
+    sh.n_tiles = list_tiles(c.n_cand);
+    sh.n_slots = std::max<int64_t>(
+        1, std::min({(int64_t(2) * device_sm_count() + n_groups - 1) /
+                         n_groups,
+                     sh.n_tiles, kMaxSlots}));
+    sh.offsets = c.cand.offsets;
+    sh.ids = c.cand.ids;
+    sh.bound_d = w.fb_d;
+    sh.bound_n = w.fb_n;
+    sh.only = w.overflow;
+    sh.k = c.k;
+    const int64_t blocks = n_groups * sh.n_slots;
+    list_scan_kernel<KPW, QG, Score>
+        <<<dim3(unsigned(blocks)), kThreads, lsmem, stream>>>(sc, w.wd, w.wn,
+                                                              sh);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    merge_kernel<KPW><<<dim3(unsigned(c.n_queries)), kThreads, 0, stream>>>(
+        w.wd, w.wn, sh, c.res.distances, c.res.nodes, c.res.counts);
+    return cudaGetLastError();
   };
-  const int qg = !shared_candidates ? 1
-                 : (kpw <= 2 && fits(8)) ? 8
-                 : (kpw <= 4 && fits(4)) ? 4
-                 : fits(2) ? 2 : 1;
-  switch (kpw) {
-    case 1:
-      return qg == 8 ? run.template go<1, 8>() : qg == 4 ? run.template go<1, 4>()
-           : qg == 2 ? run.template go<1, 2>() : run.template go<1, 1>();
-    case 2:
-      return qg == 8 ? run.template go<2, 8>() : qg == 4 ? run.template go<2, 4>()
-           : qg == 2 ? run.template go<2, 2>() : run.template go<2, 1>();
-    case 4:
-      return qg >= 4 ? run.template go<4, 4>() : qg == 2 ? run.template go<4, 2>()
-           : run.template go<4, 1>();
-    default:
-      return qg >= 2 ? run.template go<8, 2>() : run.template go<8, 1>();
+  switch (kpw_for(c.k)) {
+    case 1: return go(std::integral_constant<int, 1>());
+    case 2: return go(std::integral_constant<int, 2>());
+    case 4: return go(std::integral_constant<int, 4>());
+    default: return go(std::integral_constant<int, 8>());
   }
 }
 
+// Queries per CTA: up to 8, no more than needed for the queries, with their
+// vectors or tables and the re-scan's merge area within 200 KB of shared
+// memory, for scans of every row; 1 for per-query candidate lists.
+int group_for(int64_t n_queries, bool shared_candidates,
+              size_t per_query_bytes, int k) {
+  if (!shared_candidates) return 1;
+  const size_t lists = size_t(kWarps) * kpw_for(k) * 32 * 8;
+  int qg = 8;
+  while (qg > 1 && (qg / 2 >= n_queries ||
+                    size_t(qg) * (per_query_bytes + lists) >
+                        size_t(200) * 1024))
+    qg /= 2;
+  return qg;
+}
+
+template <template <int> class Run, typename... A>
+cudaError_t by_group(int qg, A... args) {
+  switch (qg) {
+    case 8: return Run<8>::go(args...);
+    case 4: return Run<4>::go(args...);
+    case 2: return Run<2>::go(args...);
+    default: return Run<1>::go(args...);
+  }
+}
+
+template <int QG>
 struct L2Run {
-  const vectra_scan_l2_args* a;
-  const ScanShape* sh;
-  const Workspace* w;
-  cudaStream_t stream;
-  template <int KPW, int QG>
-  cudaError_t go() const { return run_l2<KPW, QG>(a, *sh, *w, stream); }
-};
-struct PqRun {
-  const vectra_scan_pq_args* a;
-  const ScanShape* sh;
-  const Workspace* w;
-  cudaStream_t stream;
-  template <int KPW, int QG>
-  cudaError_t go() const { return run_pq<KPW, QG>(a, *sh, *w, stream); }
+  static cudaError_t go(const vectra_scan_l2_args* a, const Common* c,
+                        const Workspace* w, cudaStream_t stream) {
+    L2Score<QG> sc;
+    sc.queries = a->queries;
+    sc.query_stride = a->query_stride;
+    sc.rows = a->rows;
+    sc.row_stride = a->row_stride;
+    sc.dim = a->dimension;
+    sc.vec4 = (a->dimension % 4 == 0) && (a->row_stride % 4 == 0) &&
+              (reinterpret_cast<uintptr_t>(a->rows) % 16 == 0);
+    return run_levels<QG>(sc, L2Score<QG>::smem_floats(a->dimension), *c, *w,
+                          stream);
+  }
 };
 
-// Common argument checks and the workspace layout.
+template <int QG>
+struct PqRun {
+  template <int MS>
+  static cudaError_t with(const vectra_scan_pq_args* a, const Common* c,
+                          const Workspace* w, cudaStream_t stream) {
+    PqScore<QG, MS> sc;
+    sc.tables = a->tables;
+    sc.codes = a->codes;
+    sc.code_stride = a->code_stride;
+    sc.m = a->subspaces;
+    return run_levels<QG>(sc, PqScore<QG, MS>::smem_floats(a->subspaces), *c,
+                          *w, stream);
+  }
+  static cudaError_t go(const vectra_scan_pq_args* a, const Common* c,
+                        const Workspace* w, cudaStream_t stream) {
+    const uintptr_t base = reinterpret_cast<uintptr_t>(a->codes);
+    const bool a16 = base % 16 == 0 && a->code_stride % 16 == 0;
+    const bool a8 = base % 8 == 0 && a->code_stride % 8 == 0;
+    switch (a->subspaces) {
+      case 8: return a8 ? with<8>(a, c, w, stream) : with<0>(a, c, w, stream);
+      case 16:
+        return a16 ? with<16>(a, c, w, stream) : with<0>(a, c, w, stream);
+      case 32:
+        return a16 ? with<32>(a, c, w, stream) : with<0>(a, c, w, stream);
+      case 64:
+        return a16 ? with<64>(a, c, w, stream) : with<0>(a, c, w, stream);
+      default: return with<0>(a, c, w, stream);
+    }
+  }
+};
+
+// Common argument checks; the workspace carved.
 int prepare(int64_t n_queries, int64_t n_rows, int k,
             const vectra_scan_candidates& cand,
             const vectra_scan_results& res, void* workspace,
-            size_t workspace_bytes, ScanShape* sh, Workspace* w) {
+            size_t workspace_bytes, Common* c, Workspace* w) {
   if (res.distances == nullptr || res.nodes == nullptr) return VECTRA_ERR_NULL;
-  if (n_queries < 0 || n_rows < 0 || n_rows >= 0xffffffffLL)
+  if (n_queries < 0 || n_rows < 0 || n_rows >= 0xffffffffLL ||
+      n_queries > 0x7fffffffLL)
     return VECTRA_ERR_SHAPE;
   if (k < 1 || k > VECTRA_SCAN_MAX_K) return VECTRA_ERR_UNSUPPORTED;
   if (cand.offsets != nullptr &&
-      (cand.ids == nullptr || cand.max_per_query < 0))
+      (cand.ids == nullptr || cand.max_per_query < 0 ||
+       cand.max_per_query >= 0xffffffffLL))
     return VECTRA_ERR_NULL;
   const int64_t nc = cand.offsets == nullptr ? n_rows : cand.max_per_query;
   if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
       workspace_bytes < workspace_for(n_queries, nc, k))
     return VECTRA_ERR_NULL;
-  sh->n_queries = n_queries;
-  sh->n_rows = n_rows;
-  sh->n_tiles = tiles_for(nc);
-  sh->scan_tiles = sh->n_tiles;
-  sh->n_slots = 1;
-  sh->offsets = cand.offsets;
-  sh->ids = cand.ids;
-  sh->bound_d = nullptr;
-  sh->bound_n = nullptr;
-  sh->k = k;
-  const size_t lists = size_t(n_queries) *
-                       size_t(std::min(sh->n_tiles, kMaxSlots)) *
-                       size_t(kpw_for(k)) * 32;
-  const size_t bytes = (lists * 4 + 15) & ~size_t(15);
-  char* base = static_cast<char*>(workspace);
-  w->wd = reinterpret_cast<float*>(base);
-  w->wn = reinterpret_cast<uint32_t*>(base + bytes);
-  w->bound_d = reinterpret_cast<float*>(base + 2 * bytes);
-  w->bound_n = reinterpret_cast<uint32_t*>(base + 2 * bytes +
-                                           size_t(n_queries) * 4);
+  c->n_queries = n_queries;
+  c->n_rows = n_rows;
+  c->n_cand = nc;
+  c->cand = cand;
+  c->res = res;
+  c->k = k;
+  *w = carve(workspace, n_queries, nc, k);
   return VECTRA_OK;
 }
 
@@ -923,19 +1357,17 @@ VECTRA_API int vectra_scan_l2_topk(const vectra_scan_l2_args* a,
       a->query_stride < a->dimension || a->row_stride < a->dimension)
     return VECTRA_ERR_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ScanShape sh;
+  Common c;
   Workspace w;
   const int st = prepare(a->n_queries, a->n_rows, a->k, a->candidates,
-                         a->results, a->workspace, a->workspace_bytes, &sh,
+                         a->results, a->workspace, a->workspace_bytes, &c,
                          &w);
   if (st != VECTRA_OK) return st;
   if (a->n_queries == 0) return VECTRA_OK;
-  const int dpad = (a->dimension + 3) & ~3;
-  L2Run run{a, &sh, &w, s};
-  return by_kpw(a->k, a->candidates.offsets == nullptr, dpad, run) ==
-                 cudaSuccess
-             ? VECTRA_OK
-             : VECTRA_ERR_CUDA;
+  const int qg = group_for(a->n_queries, a->candidates.offsets == nullptr,
+                           size_t((a->dimension + 3) & ~3) * 4, a->k);
+  return by_group<L2Run>(qg, a, &c, &w, s) == cudaSuccess ? VECTRA_OK
+                                                          : VECTRA_ERR_CUDA;
 }
 
 VECTRA_API int vectra_scan_pq_topk(const vectra_scan_pq_args* a,
@@ -946,18 +1378,18 @@ VECTRA_API int vectra_scan_pq_topk(const vectra_scan_pq_args* a,
       a->code_stride < a->subspaces)
     return VECTRA_ERR_SHAPE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ScanShape sh;
+  Common c;
   Workspace w;
   const int st = prepare(a->n_queries, a->n_rows, a->k, a->candidates,
-                         a->results, a->workspace, a->workspace_bytes, &sh,
+                         a->results, a->workspace, a->workspace_bytes, &c,
                          &w);
   if (st != VECTRA_OK) return st;
   if (a->n_queries == 0) return VECTRA_OK;
-  PqRun run{a, &sh, &w, s};
-  return by_kpw(a->k, a->candidates.offsets == nullptr,
-                a->subspaces * VECTRA_PQ_CENTROIDS, run) == cudaSuccess
-             ? VECTRA_OK
-             : VECTRA_ERR_CUDA;
+  const int qg = group_for(a->n_queries, a->candidates.offsets == nullptr,
+                           size_t(a->subspaces) * VECTRA_PQ_CENTROIDS * 4,
+                           a->k);
+  return by_group<PqRun>(qg, a, &c, &w, s) == cudaSuccess ? VECTRA_OK
+                                                          : VECTRA_ERR_CUDA;
 }
 
 VECTRA_API int vectra_scan_l2_topk_noalloc(const vectra_scan_l2_args* a,
