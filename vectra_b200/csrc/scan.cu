@@ -22,11 +22,11 @@
 //    ballot and one atomic per warp); its select lowers the bound again.
 //    Sample sizes are planned so that the last level admits a few thousand
 //    candidates per query out of millions.
-//  * Select: one CTA of 1,024 threads per query holds the buffer's keys in
-//    registers and radix-selects the k-th (key, node) value with 11-bit
-//    digits (a shared-memory histogram per digit) until the entries at or
-//    under the current digit bucket fit a 2,048-entry bitonic sort; the
-//    sorted head is the result.
+//  * Select: one CTA of 1,024 threads per query stages the buffer's keys in
+//    shared memory; one histogram over their range (2,048 bins) usually
+//    leaves few enough entries at or under the bin of the k-th to sort
+//    (bitonic, in one warp up to 256); otherwise a radix select over 11-bit
+//    digits of (key, node) narrows them first.
 //  * A last level that admits more candidates than its buffer holds (mass
 //    ties at the bound) is redone for that query by the warp-list scan:
 //    per-warp sorted lists in registers fed by ballot-filtered insertion,
@@ -58,7 +58,6 @@ constexpr unsigned kFull = 0xffffffffu;
 // Candidate buffer per query (entries), and the select kernel's shape.
 constexpr int64_t kCap = 32768;
 constexpr int kSelThreads = 1024;
-constexpr int kSelKeys = int(kCap / kSelThreads);
 constexpr int kSortMax = 2048;
 // Candidates scored by level 0 when a query has more than kCap.
 constexpr int64_t kSample0 = 8192;
@@ -442,10 +441,66 @@ __device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t* wtot,
   return r;
 }
 
+// Bitonic sort, ascending, of p2 (a power of two) values in shared memory
+// by threads t = 0 .. nt - 1: one warp (WARP, __syncwarp between stages) or
+// the whole block (__syncthreads).
+template <bool WARP>
+__device__ __forceinline__ void smem_bitonic(unsigned long long* v,
+                                             uint32_t p2, uint32_t t,
+                                             uint32_t nt) {
+#pragma unroll 1
+  for (uint32_t size = 2; size <= p2; size <<= 1) {
+#pragma unroll 1
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll 1
+      for (uint32_t i = t; i < p2 / 2; i += nt) {
+        const uint32_t lo = (i / stride) * 2 * stride + (i % stride);
+        const uint32_t hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const unsigned long long x = v[lo], y = v[hi];
+        if ((x > y) == up) {
+          v[lo] = y;
+          v[hi] = x;
+        }
+      }
+      if (WARP) {
+        __syncwarp();
+      } else {
+        __syncthreads();
+      }
+    }
+  }
+}
+
+// The bin of 2 * tid or 2 * tid + 1 holding rank r (from 1) of a histogram
+// (2,048 bins, two per thread): pick = (bin, entries before it, in it).
+__device__ __forceinline__ void pick_bin(const uint32_t* hist, uint32_t r,
+                                         uint32_t* wtot, uint32_t* pick) {
+  const int tid = threadIdx.x;
+  const uint32_t h0 = hist[2 * tid], h1 = hist[2 * tid + 1];
+  uint32_t total;
+  const uint32_t ex = block_scan(h0 + h1, wtot, &total);
+  if (ex < r && r <= ex + h0) {
+    pick[0] = 2 * tid;
+    pick[1] = ex;
+    pick[2] = h0;
+  } else if (ex + h0 < r && r <= ex + h0 + h1) {
+    pick[0] = 2 * tid + 1;
+    pick[1] = ex + h0;
+    pick[2] = h1;
+  }
+}
+
+// One CTA per query. The buffer's keys are staged in shared memory; loops
+// stay rolled (each launch runs its code once, so a short kernel starts
+// sooner).
 __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
+  extern __shared__ uint32_t skey[];  // [cap]
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t wtot[33];
   __shared__ uint32_t pick[3];
+  __shared__ uint32_t span[64];
+  __shared__ uint32_t n_sel_sh;
   __shared__ unsigned long long sorted[kSortMax];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t q = blockIdx.x;
@@ -453,25 +508,21 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
   const int64_t n = int64_t(n_total) < a.cap ? int64_t(n_total) : a.cap;
   const uint32_t* qk = a.keys + q * a.cap;
   const uint32_t* qn = a.nodes + q * a.cap;
-  uint32_t key[kSelKeys];
-#pragma unroll
-  for (int i = 0; i < kSelKeys; ++i) {
-    const int64_t idx = int64_t(i) * kSelThreads + tid;
-    key[i] = idx < n ? qk[idx] : kNoBound;
-  }
+#pragma unroll 4
+  for (int64_t i = tid; i < n; i += kSelThreads) skey[i] = qk[i];
   hist[tid] = 0u;
   hist[tid + kSelThreads] = 0u;
+  if (tid == 0) n_sel_sh = 0u;
   __syncthreads();  // every thread has read the count
   if (tid == 0) a.count[q] = 0u;  // the next level appends from zero
   const uint32_t need = uint32_t(int64_t(a.k) < n ? int64_t(a.k) : n);
   if (a.mode == kFinal) {
     const bool over = n_total > a.cap;
     if (tid == 0) {
-      // The re-scan's bound: this query's, or none admitted when it is not
-      // re-scanned (its CTAs may still run beside a query that is).
+      // The re-scan runs only where this is set; it takes no bound (its
+      // distances may round differently from the levels').
       a.overflow[q] = over ? 1 : 0;
-      const uint32_t b = a.bound[q];
-      a.fb_d[q] = !over ? -INFINITY : b == kNoBound ? INFINITY : key_dist(b);
+      a.fb_d[q] = over ? INFINITY : -INFINITY;
       a.fb_n[q] = kNoNode;
     }
     if (over) return;  // the warp-list re-scan writes this query
@@ -488,31 +539,68 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
     return;
   }
 
-  // Radix select of the need-th smallest (key << 32 | node): 11/11/10-bit
-  // digits of the key, then of the node, until the entries at or under the
-  // bucket fit the sort buffer.
+  // First one histogram of the keys' offsets from their smallest, in 2,048
+  // bins spanning their range: when the entries before the end of the bin
+  // holding the need-th fit the sort buffer, those are gathered (ranged).
+  bool ranged = false;
+  uint64_t range_end = 0;  // ranged: the keys under it are gathered
+  if (n > kSortMax) {
+    uint32_t lo = kNoBound, hi = 0u;
+#pragma unroll 4
+    for (int64_t i = tid; i < n; i += kSelThreads) {
+      lo = umin(lo, skey[i]);
+      hi = umax(hi, skey[i]);
+    }
+    lo = __reduce_min_sync(kFull, lo);
+    hi = __reduce_max_sync(kFull, hi);
+    if (lane == 0) {
+      span[warp] = lo;
+      span[32 + warp] = hi;
+    }
+    __syncthreads();
+    lo = __reduce_min_sync(kFull, span[lane]);
+    hi = __reduce_max_sync(kFull, span[32 + lane]);
+    const uint32_t range = hi - lo;
+    const int shift = range < 2048u ? 0 : 32 - __clz(range) - 11;
+#pragma unroll 4
+    for (int64_t i = tid; i < n; i += kSelThreads)
+      atomicAdd(&hist[(skey[i] - lo) >> shift], 1u);
+    __syncthreads();
+    pick_bin(hist, need, wtot, pick);
+    hist[2 * tid] = 0u;
+    hist[2 * tid + 1] = 0u;
+    __syncthreads();
+    ranged = pick[1] + pick[2] <= uint32_t(kSortMax);
+    range_end = uint64_t(lo) + (uint64_t(pick[0] + 1) << shift);
+    __syncthreads();  // pick is rewritten below
+  }
+
+  // Otherwise a radix select of the need-th smallest (key << 32 | node):
+  // 11/11/10-bit digits of the key, then of the node, until the entries at
+  // or under the bucket fit the sort buffer.
   uint64_t pre = 0;      // the selected digits so far, in place
   int pbits = 0;         // how many top bits they fix
   uint32_t below = 0;    // entries under the bucket
   uint32_t in_bucket = uint32_t(n);
-  for (int round = 0; round < 6 && below + in_bucket > uint32_t(kSortMax);
+#pragma unroll 1
+  for (int round = 0;
+       !ranged && round < 6 && below + in_bucket > uint32_t(kSortMax);
        ++round) {
     const int w = round % 3 == 2 ? 10 : 11;
     const int shift = 64 - pbits - w;
     const uint32_t pk32 = uint32_t(pre >> 32);
-#pragma unroll
-    for (int i = 0; i < kSelKeys; ++i) {
-      if (int64_t(i) * kSelThreads + warp * 32 >= n) break;  // warp-uniform
-      const int64_t idx = int64_t(i) * kSelThreads + tid;
+#pragma unroll 1
+    for (int64_t base = int64_t(warp) * 32; base < n; base += kSelThreads) {
+      const int64_t idx = base + lane;  // the warp iterates together
       bool inb = idx < n;
       uint32_t bin = 0;
       if (inb) {
+        const uint32_t kv = skey[idx];
         if (pbits < 32) {
-          inb = pbits == 0 ||
-                (key[i] >> (32 - pbits)) == (pk32 >> (32 - pbits));
-          bin = (key[i] >> (shift - 32)) & ((1u << w) - 1u);
+          inb = pbits == 0 || (kv >> (32 - pbits)) == (pk32 >> (32 - pbits));
+          bin = (kv >> (shift - 32)) & ((1u << w) - 1u);
         } else {
-          inb = key[i] == pk32;
+          inb = kv == pk32;
           if (inb) {
             const uint32_t nd = qn[idx];
             const int nb = pbits - 32;
@@ -529,19 +617,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
       }
     }
     __syncthreads();
-    const uint32_t h0 = hist[2 * tid], h1 = hist[2 * tid + 1];
-    uint32_t total;
-    const uint32_t ex = block_scan(h0 + h1, wtot, &total);
-    const uint32_t r = need - below;  // rank inside the bucket, from 1
-    if (ex < r && r <= ex + h0) {
-      pick[0] = 2 * tid;
-      pick[1] = ex;
-      pick[2] = h0;
-    } else if (ex + h0 < r && r <= ex + h0 + h1) {
-      pick[0] = 2 * tid + 1;
-      pick[1] = ex + h0;
-      pick[2] = h1;
-    }
+    pick_bin(hist, need - below, wtot, pick);
     hist[2 * tid] = 0u;
     hist[2 * tid + 1] = 0u;
     __syncthreads();
@@ -554,57 +630,55 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
 
   // Gather the entries at or under the bucket (strictly under it when they
   // are copies of one value beyond the buffer) and sort them.
-  const bool copies = below + in_bucket > uint32_t(kSortMax);
+  const bool copies = !ranged && below + in_bucket > uint32_t(kSortMax);
   const uint32_t pk32 = uint32_t(pre >> 32), pn32 = uint32_t(pre);
-  uint32_t sel = 0u;
-#pragma unroll
-  for (int i = 0; i < kSelKeys; ++i) {
-    const int64_t idx = int64_t(i) * kSelThreads + tid;
-    if (idx >= n) break;
-    bool s;
-    if (pbits == 0) {
-      s = true;
-    } else if (pbits <= 32) {
-      s = (key[i] >> (32 - pbits)) <= (pk32 >> (32 - pbits));
-    } else if (key[i] != pk32) {
-      s = key[i] < pk32;
-    } else {
-      const uint32_t nd = qn[idx];
-      s = copies ? nd < pn32 : (nd >> (64 - pbits)) <= (pn32 >> (64 - pbits));
+#pragma unroll 1
+  for (int64_t base = int64_t(warp) * 32; base < n; base += kSelThreads) {
+    const int64_t idx = base + lane;
+    bool s = false;
+    uint32_t kv = 0u, nd = 0u;
+    if (idx < n) {
+      kv = skey[idx];
+      if (ranged) {
+        s = uint64_t(kv) < range_end;
+      } else if (pbits == 0) {
+        s = true;
+      } else if (pbits <= 32) {
+        s = (kv >> (32 - pbits)) <= (pk32 >> (32 - pbits));
+      } else if (kv != pk32) {
+        s = kv < pk32;
+      } else {
+        nd = qn[idx];
+        s = copies ? nd < pn32 : (nd >> (64 - pbits)) <= (pn32 >> (64 - pbits));
+      }
     }
-    if (s) sel |= 1u << i;
+    const unsigned bal = __ballot_sync(kFull, s);
+    if (bal == 0u) continue;
+    const int leader = __ffs(bal) - 1;
+    uint32_t pos = 0u;
+    if (lane == leader) pos = atomicAdd(&n_sel_sh, uint32_t(__popc(bal)));
+    pos = __shfl_sync(kFull, pos, leader) +
+          uint32_t(__popc(bal & ((1u << lane) - 1u)));
+    if (s && pos < uint32_t(kSortMax))
+      sorted[pos] = (uint64_t(kv) << 32) | qn[idx];
   }
-  uint32_t n_sel;
-  uint32_t off = block_scan(uint32_t(__popc(sel)), wtot, &n_sel);
-#pragma unroll
-  for (int i = 0; i < kSelKeys; ++i) {
-    if (sel & (1u << i)) {
-      if (off < uint32_t(kSortMax))
-        sorted[off] = (uint64_t(key[i]) << 32) |
-                      qn[int64_t(i) * kSelThreads + tid];
-      ++off;
-    }
-  }
-  n_sel = n_sel < uint32_t(kSortMax) ? n_sel : uint32_t(kSortMax);
+  __syncthreads();
+  const uint32_t n_sel = n_sel_sh < uint32_t(kSortMax) ? n_sel_sh
+                                                       : uint32_t(kSortMax);
   uint32_t p2 = 2;
   while (p2 < n_sel) p2 <<= 1;
-  for (uint32_t i = n_sel + tid; i < p2; i += kSelThreads) sorted[i] = ~0ull;
-  __syncthreads();
-  for (uint32_t size = 2; size <= p2; size <<= 1) {
-    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-      for (uint32_t i = tid; i < p2 / 2; i += kSelThreads) {
-        const uint32_t lo = (i / stride) * 2 * stride + (i % stride);
-        const uint32_t hi = lo + stride;
-        const bool up = (lo & size) == 0;
-        const unsigned long long x = sorted[lo], y = sorted[hi];
-        if ((x > y) == up) {
-          sorted[lo] = y;
-          sorted[hi] = x;
-        }
-      }
-      __syncthreads();
+  if (p2 <= 256u) {  // one warp sorts
+    if (warp == 0) {
+      for (uint32_t i = n_sel + lane; i < p2; i += 32) sorted[i] = ~0ull;
+      __syncwarp();
+      smem_bitonic<true>(sorted, p2, lane, 32);
     }
+  } else {
+    for (uint32_t i = n_sel + tid; i < p2; i += kSelThreads) sorted[i] = ~0ull;
+    __syncthreads();
+    smem_bitonic<false>(sorted, p2, tid, kSelThreads);
   }
+  __syncthreads();
   if (a.mode != kFinal) {
     if (tid == 0) {
       const uint32_t kth =
@@ -1083,9 +1157,14 @@ cudaError_t prepare_kernel(const void* kern, size_t smem, int threads,
     }
   }
   cudaError_t err = cudaSuccess;
-  if (!attr)
+  if (!attr) {
+    // Up to 227 KB per block, static shared memory included.
+    cudaFuncAttributes fa;
+    if ((err = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return err;
     err = cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        int(227 * 1024 - fa.sharedSizeBytes));
+  }
   if (err != cudaSuccess) return err;
   int blocks = 0;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, threads,
@@ -1117,6 +1196,11 @@ cudaError_t run_levels(const Score& sc, size_t smem_floats, const Common& c,
   cudaError_t err = prepare_kernel(
       reinterpret_cast<const void*>(level_kernel<QG, Score>), smem, kThreads,
       &per_sm);
+  if (err != cudaSuccess) return err;
+  const size_t sel_smem = size_t(p.cap) * 4;
+  int sel_per_sm = 1;
+  err = prepare_kernel(reinterpret_cast<const void*>(select_kernel), sel_smem,
+                       kSelThreads, &sel_per_sm);
   if (err != cudaSuccess) return err;
   const int64_t n_groups = (c.n_queries + QG - 1) / QG;
   const int64_t target = std::max<int64_t>(
@@ -1162,7 +1246,8 @@ cudaError_t run_levels(const Score& sc, size_t smem_floats, const Common& c,
     s.overflow = w.overflow;
     s.fb_d = w.fb_d;
     s.fb_n = w.fb_n;
-    select_kernel<<<dim3(unsigned(c.n_queries)), kSelThreads, 0, stream>>>(s);
+    select_kernel<<<dim3(unsigned(c.n_queries)), kSelThreads, sel_smem,
+                    stream>>>(s);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
   if (!p.rescan) return cudaSuccess;
