@@ -296,3 +296,24 @@ def test_duplicate_candidate_ids_are_kept_like_the_reference_heap():
     lists = [np.concatenate([np.full(copies, best), rng.choice(50000, 500)])
              for copies in (7, 3000, 40000)]  # sorted, past the sort, re-scan
     _pq_check(tables, codes, 30, lists)
+
+
+@pytest.mark.parametrize('nq,d', [(3, 256), (8, 64), (2, 192), (5, 128)])
+def test_l2_bulk_copy_shapes(nq, d):
+    # dim = 64 NC with aligned rows runs the bulk-copy level kernel (NC 1,
+    # 2, 4); 192 (NC 3) runs the lane-per-row one.
+    _l2_random(nq, 70000, d, 48, seed=d + nq)
+
+
+def test_l2_bulk_copy_row_stride_and_tail():
+    rng = np.random.default_rng(26)
+    base = torch.from_numpy(rng.standard_normal((50001, 132)).astype(
+        np.float32)).cuda()
+    rows = base[:, :128]  # stride 132 floats, 50,001 rows (a ragged batch)
+    queries = (base[7:11, :128] + 0.05).contiguous()
+    gd, gn, gc = scan.l2_topk(queries, rows, 33)
+    for qi in range(4):
+        wd, wn = scan_oracle.exhaustive_l2_topk(
+            queries[qi].cpu().numpy(), rows.cpu().numpy(), 33)
+        _check_l2(gd[qi].cpu().numpy(), gn[qi].cpu().numpy(), 33, wd, wn,
+                  queries[qi].cpu().numpy(), rows.cpu().numpy(), 128)

@@ -155,19 +155,6 @@ int select(const RbfProblem& p, uint32_t flags) {
   return VECTRA_KERNEL_GENERIC;
 }
 
-// Device address of the error word on the current device (cached).
-unsigned int* device_error_ptr() {
-  const int dev = current_device();
-  if (dev < 0 || dev >= kMaxDevices) return nullptr;
-  unsigned int* ptr = g_err_ptr[dev].load(std::memory_order_acquire);
-  if (ptr) return ptr;
-  void* addr = nullptr;
-  if (cudaGetSymbolAddress(&addr, g_vectra_device_error) != cudaSuccess)
-    return nullptr;
-  ptr = static_cast<unsigned int*>(addr);
-  g_err_ptr[dev].store(ptr, std::memory_order_release);
-  return ptr;
-}
 
 }  // namespace
 
@@ -187,6 +174,24 @@ int device_sm_count() {
 }  // namespace vectra
 
 using namespace vectra;
+
+namespace vectra {
+
+// Device address of the error word on the current device (cached).
+unsigned int* device_error_ptr() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  unsigned int* ptr = g_err_ptr[dev].load(std::memory_order_acquire);
+  if (ptr) return ptr;
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_vectra_device_error) != cudaSuccess)
+    return nullptr;
+  ptr = static_cast<unsigned int*>(addr);
+  g_err_ptr[dev].store(ptr, std::memory_order_release);
+  return ptr;
+}
+
+}  // namespace vectra
 
 extern "C" {
 

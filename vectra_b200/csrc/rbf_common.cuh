@@ -360,4 +360,9 @@ bool make_tile_map(CUtensorMap* map, const void* base, int dtype, int64_t B,
 // Streaming-multiprocessor count of the current device (cached).
 int device_sm_count();
 
+// Device address of the library's error word on the current device (cached;
+// null when it cannot be looked up). Kernels set kErr* bits there;
+// vectra_rbf_check_device_errors reads and clears it.
+unsigned int* device_error_ptr();
+
 }  // namespace vectra

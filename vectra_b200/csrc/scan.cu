@@ -391,6 +391,223 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // ---------------------------------------------------------------------------
+// L2 levels over every row or a sample of groups of consecutive rows (no
+// candidate lists), with dim = 64 * NC: rows reach shared memory by bulk
+// copy and 16 lanes share a row.
+//  * Each warp streams its own contiguous run of the CTA tile in batches of
+//    8 consecutive rows (8 * row_stride floats), kBulkStages copies in
+//    flight (one mbarrier each; waits bounded, timeouts set the device
+//    error word).
+//  * Half-warp h of a step takes row 2 * step + h of the batch; lane
+//    l16 = lane % 16 holds floats [64 c + 4 l16, 64 c + 4 l16 + 4) of chunk
+//    c of the row and of each of the QG queries (queries in registers).
+//  * The 16 partial sums per query are added by a transposing butterfly
+//    (each exchange halves the values a lane keeps), so a lane ends with the
+//    full distance of one (row, query); its owner lane stores or appends it.
+// ---------------------------------------------------------------------------
+constexpr int kBulkRows = 8;
+constexpr int kBulkStages = 3;
+
+struct L2Bulk {
+  const float* queries;
+  int64_t query_stride;
+  const float* rows;
+  int64_t row_stride;  // floats; a multiple of 4
+  unsigned int* err;
+};
+
+// Sum over the 16 lanes of a half-warp of v[g] (g < QG): the lane's result
+// is the sum for query *g, which it returns.
+template <int QG>
+__device__ __forceinline__ float half_warp_reduce(float (&v)[QG], int lane,
+                                                  int* g) {
+  int base = 0;
+  int cnt = QG;
+#pragma unroll
+  for (int m = 8; m >= 1; m >>= 1) {
+    if (cnt >= 2) {
+      const int h = cnt / 2;
+      const bool up = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const float send = up ? v[i] : v[i + h];
+        const float keep = up ? v[i + h] : v[i];
+        v[i] = keep + __shfl_xor_sync(kFull, send, m);
+      }
+      if (up) base += h;
+      cnt = h;
+    } else {
+      v[0] += __shfl_xor_sync(kFull, v[0], m);
+    }
+  }
+  *g = base;
+  return v[0];
+}
+
+template <int QG, int NC>
+__global__ void __launch_bounds__(kThreads, 2)
+    l2_bulk_kernel(L2Bulk b, Level L) {
+  extern __shared__ __align__(128) unsigned char smem_b[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n_groups = (L.n_queries + QG - 1) / QG;
+  const int64_t group = blockIdx.x % n_groups;
+  const int64_t slot = blockIdx.x / n_groups;
+  const int64_t q0 = group * QG;
+  const int64_t n = L.n_rows;
+  const bool every = L.groups == 0 || 32 * L.groups >= n;
+  const int64_t m = every ? n : 32 * L.groups;
+  const int64_t spacing = every ? 0 : n / L.groups;
+  const int64_t tile = int64_t(kThreads) * L.rows_per_lane;
+  const bool store_all = L.bound == nullptr;
+  if (store_all && slot == 0 && threadIdx.x < QG &&
+      q0 + threadIdx.x < L.n_queries)
+    L.count[q0 + threadIdx.x] = uint32_t(m < L.cap ? m : L.cap);
+  if (slot * tile >= m) return;
+
+  const uint32_t stage_bytes =
+      uint32_t(kBulkRows * b.row_stride * sizeof(float));
+  float* wbuf = reinterpret_cast<float*>(smem_b) +
+                size_t(warp) * kBulkStages * kBulkRows * b.row_stride;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      smem_b + size_t(kWarps) * kBulkStages * stage_bytes);
+  const uint32_t bar0 = smem_addr(bars + warp * kBulkStages);
+  if (lane == 0) {
+#pragma unroll
+    for (int st = 0; st < kBulkStages; ++st) mbar_init(bar0 + 8 * st, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  // Queries: chunk c, lane slice l16, as packed pairs.
+  const int l16 = lane & 15, half = lane >> 4;
+  uint64_t qp[QG][NC][2];
+#pragma unroll
+  for (int g = 0; g < QG; ++g)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (q0 + g < L.n_queries) {
+        const float* qs = b.queries + (q0 + g) * b.query_stride + 64 * c +
+                          4 * l16;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = __ldg(qs + e);
+      }
+      qp[g][c][0] = pk(v[0], v[1]);
+      qp[g][c][1] = pk(v[2], v[3]);
+    }
+  // This lane's query after the reduction, and which lanes own a result.
+  int my_g = 0;
+  {
+    float probe[QG];
+#pragma unroll
+    for (int g = 0; g < QG; ++g) probe[g] = 0.f;
+    half_warp_reduce<QG>(probe, lane, &my_g);
+  }
+  constexpr int kDupMask = QG >= 8 ? 1 : QG == 4 ? 3 : QG == 2 ? 7 : 15;
+  const bool owner = (lane & kDupMask) == 0 && q0 + my_g < L.n_queries;
+  const int64_t my_q = q0 + my_g;
+  const uint32_t my_bound =
+      (!store_all && owner) ? L.bound[my_q] : kNoBound;
+
+  // The warp's batches: in tile t, scan indices [t * tile + warp * run,
+  // + run) in batches of 8; they stay below m for a prefix of the sequence.
+  const int64_t run = tile / kWarps;
+  const int64_t per_tile = run / kBulkRows;
+  auto batch_j0 = [&](int64_t u) {
+    const int64_t t = slot + (u / per_tile) * L.n_slots;
+    return t * tile + warp * run + (u % per_tile) * kBulkRows;
+  };
+  const uint64_t policy = l2_evict_first_policy();
+  auto issue = [&](int64_t u) {  // lane 0
+    const int64_t j0 = batch_j0(u);
+    const int64_t nv = m - j0 < kBulkRows ? m - j0 : kBulkRows;
+    const int64_t i0 = every ? j0 : (j0 >> 5) * spacing + (j0 & 31);
+    const int st = int(u % kBulkStages);
+    const uint32_t bytes = uint32_t(nv * b.row_stride * sizeof(float));
+    mbar_arrive_expect_tx(bar0 + 8 * st, bytes);
+    bulk_g2s(smem_addr(wbuf + size_t(st) * kBulkRows * b.row_stride),
+             b.rows + i0 * b.row_stride, bytes, bar0 + 8 * st, policy);
+  };
+  int64_t issued = 0;  // the same on every lane
+  for (; issued < kBulkStages && batch_j0(issued) < m; ++issued)
+    if (lane == 0) issue(issued);
+
+  bool failed = false;
+  int64_t u = 0;
+  for (; batch_j0(u) < m; ++u) {
+    const int st = int(u % kBulkStages);
+    const uint32_t phase = uint32_t((u / kBulkStages) & 1);
+    if (!mbar_wait(bar0 + 8 * st, phase, b.err)) {
+      failed = true;
+      ++u;
+      break;
+    }
+    const int64_t j0 = batch_j0(u);
+    const float* sb = wbuf + size_t(st) * kBulkRows * b.row_stride;
+#pragma unroll 1
+    for (int step = 0; step < kBulkRows / 2; ++step) {
+      const int r = 2 * step + half;
+      const float* row = sb + r * b.row_stride + 4 * l16;
+      uint64_t acc[QG];
+#pragma unroll
+      for (int g = 0; g < QG; ++g) acc[g] = 0;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const float4 rv = *reinterpret_cast<const float4*>(row + 64 * c);
+        const uint64_t r01 = pk(rv.x, rv.y), r23 = pk(rv.z, rv.w);
+#pragma unroll
+        for (int g = 0; g < QG; ++g) {
+          const uint64_t d01 = sub2(qp[g][c][0], r01);
+          const uint64_t d23 = sub2(qp[g][c][1], r23);
+          acc[g] = fma2(d01, d01, acc[g]);
+          acc[g] = fma2(d23, d23, acc[g]);
+        }
+      }
+      float part[QG];
+#pragma unroll
+      for (int g = 0; g < QG; ++g) {
+        const float2 a2 = upk(acc[g]);
+        part[g] = a2.x + a2.y;
+      }
+      int gq;
+      const float dist = half_warp_reduce<QG>(part, lane, &gq);
+      const int64_t j = j0 + r;
+      if (!owner || j >= m) continue;
+      const uint32_t key = dist_key(dist);
+      const uint32_t node =
+          uint32_t(every ? j : (j >> 5) * spacing + (j & 31));
+      uint32_t* qk = L.keys + my_q * L.cap;
+      uint32_t* qn = L.nodes + my_q * L.cap;
+      if (store_all) {
+        if (j < L.cap) {
+          qk[j] = key;
+          qn[j] = node;
+        }
+      } else if (key <= my_bound) {
+        const uint32_t pos = atomicAdd(L.count + my_q, 1u);
+        if (pos < L.cap) {
+          qk[pos] = key;
+          qn[pos] = node;
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with the stage
+    if (batch_j0(issued) < m) {  // refill it
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        issue(issued);
+      }
+      ++issued;
+    }
+  }
+  if (failed) {  // let the copies still in flight land before returning
+    for (; u < issued; ++u)
+      mbar_wait(bar0 + 8 * int(u % kBulkStages),
+                uint32_t((u / kBulkStages) & 1), b.err);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Select: the k smallest (key, node) values of a query's buffer.
 // ---------------------------------------------------------------------------
 enum SelectMode { kFirstBound = 0, kLowerBound = 1, kFinal = 2 };
@@ -1187,15 +1404,43 @@ struct Common {
 
 // The levels and selects of one scan, then the warp-list re-scan of the
 // queries whose last level overflowed (its CTAs return at once otherwise).
+// Level launches: the lane-per-row kernel (any scorer, candidate lists) ...
 template <int QG, class Score>
-cudaError_t run_levels(const Score& sc, size_t smem_floats, const Common& c,
+struct LaneLevels {
+  Score sc;
+  size_t smem;
+  cudaError_t prepare(int* per_sm) const {
+    return prepare_kernel(
+        reinterpret_cast<const void*>(level_kernel<QG, Score>), smem,
+        kThreads, per_sm);
+  }
+  void launch(unsigned blocks, const Level& L, cudaStream_t stream) const {
+    level_kernel<QG, Score><<<dim3(blocks), kThreads, smem, stream>>>(sc, L);
+  }
+};
+
+// ... or the bulk-copy L2 kernel.
+template <int QG, int NC>
+struct BulkLevels {
+  L2Bulk b;
+  size_t smem;
+  cudaError_t prepare(int* per_sm) const {
+    return prepare_kernel(reinterpret_cast<const void*>(l2_bulk_kernel<QG, NC>),
+                          smem, kThreads, per_sm);
+  }
+  void launch(unsigned blocks, const Level& L, cudaStream_t stream) const {
+    l2_bulk_kernel<QG, NC><<<dim3(blocks), kThreads, smem, stream>>>(b, L);
+  }
+};
+
+template <int QG, class Score, class Levels>
+cudaError_t run_levels(const Score& sc, size_t smem_floats,
+                       const Levels& levels, const Common& c,
                        const Workspace& w, cudaStream_t stream) {
   const Plan p = plan_for(c.n_cand, c.k);
-  const size_t smem = smem_floats * 4;
+  const size_t smem = smem_floats * 4;  // the scorer's (re-scan kernel)
   int per_sm = 1;
-  cudaError_t err = prepare_kernel(
-      reinterpret_cast<const void*>(level_kernel<QG, Score>), smem, kThreads,
-      &per_sm);
+  cudaError_t err = levels.prepare(&per_sm);
   if (err != cudaSuccess) return err;
   const size_t sel_smem = size_t(p.cap) * 4;
   int sel_per_sm = 1;
@@ -1229,8 +1474,7 @@ cudaError_t run_levels(const Score& sc, size_t smem_floats, const Common& c,
     L.cap = p.cap;
     const int64_t blocks = n_groups * L.n_slots;
     if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-    level_kernel<QG, Score>
-        <<<dim3(unsigned(blocks)), kThreads, smem, stream>>>(sc, L);
+    levels.launch(unsigned(blocks), L, stream);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     Select s;
     s.cap = p.cap;
@@ -1329,8 +1573,34 @@ struct L2Run {
     sc.dim = a->dimension;
     sc.vec4 = (a->dimension % 4 == 0) && (a->row_stride % 4 == 0) &&
               (reinterpret_cast<uintptr_t>(a->rows) % 16 == 0);
-    return run_levels<QG>(sc, L2Score<QG>::smem_floats(a->dimension), *c, *w,
-                          stream);
+    const size_t sf = L2Score<QG>::smem_floats(a->dimension);
+    // Rows of every candidate (no lists), 16-byte aligned, dim = 64 NC with
+    // the queries' slices fitting 64 registers: the bulk-copy kernel.
+    const int nc = a->dimension / 64;
+    const bool bulk = c->cand.offsets == nullptr && sc.vec4 &&
+                      a->dimension % 64 == 0 && a->row_stride <= 256 &&
+                      (nc == 1 || nc == 2 || nc == 4) && QG * nc <= 16;
+    if (bulk) {
+      L2Bulk b{a->queries, a->query_stride, a->rows, a->row_stride,
+               device_error_ptr()};
+      const size_t smem = size_t(kWarps) * kBulkStages * kBulkRows *
+                              a->row_stride * sizeof(float) +
+                          size_t(kWarps) * kBulkStages * 8;
+      if constexpr (QG <= 4) {
+        if (nc == 4)
+          return run_levels<QG>(sc, sf, BulkLevels<QG, 4>{b, smem}, *c, *w,
+                                stream);
+      }
+      if constexpr (QG <= 8) {
+        if (nc == 2)
+          return run_levels<QG>(sc, sf, BulkLevels<QG, 2>{b, smem}, *c, *w,
+                                stream);
+      }
+      return run_levels<QG>(sc, sf, BulkLevels<QG, 1>{b, smem}, *c, *w,
+                            stream);
+    }
+    return run_levels<QG>(sc, sf, LaneLevels<QG, L2Score<QG>>{sc, sf * 4}, *c,
+                          *w, stream);
   }
 };
 
@@ -1344,8 +1614,9 @@ struct PqRun {
     sc.codes = a->codes;
     sc.code_stride = a->code_stride;
     sc.m = a->subspaces;
-    return run_levels<QG>(sc, PqScore<QG, MS>::smem_floats(a->subspaces), *c,
-                          *w, stream);
+    const size_t sf = PqScore<QG, MS>::smem_floats(a->subspaces);
+    return run_levels<QG>(sc, sf, LaneLevels<QG, PqScore<QG, MS>>{sc, sf * 4},
+                          *c, *w, stream);
   }
   static cudaError_t go(const vectra_scan_pq_args* a, const Common* c,
                         const Workspace* w, cudaStream_t stream) {
