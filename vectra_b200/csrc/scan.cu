@@ -398,12 +398,18 @@ __global__ void __launch_bounds__(kThreads)
 //    8 consecutive rows (8 * row_stride floats), kBulkStages copies in
 //    flight (one mbarrier each; waits bounded, timeouts set the device
 //    error word).
-//  * Half-warp h of a step takes row 2 * step + h of the batch; lane
-//    l16 = lane % 16 holds floats [64 c + 4 l16, 64 c + 4 l16 + 4) of chunk
-//    c of the row and of each of the QG queries (queries in registers).
-//  * The 16 partial sums per query are added by a transposing butterfly
-//    (each exchange halves the values a lane keeps), so a lane ends with the
-//    full distance of one (row, query); its owner lane stores or appends it.
+//  * A step covers 4 rows of the batch: half-warp h takes rows 2 rho + h
+//    (rho = 0, 1); lane l16 = lane % 16 holds floats [64 c + 4 l16, +4) of
+//    chunk c of both rows and of each of the QG queries (in registers), so
+//    it forms 2 QG partial sums.
+//  * A butterfly over the 16 lanes adds them up: at each of the exchanges
+//    (lane distance 8, 4, 2, 1) a lane keeps half of its values and adds its
+//    partner's matching half, until one value is left. The lane's values
+//    are laid out so that the half it keeps is always the first: item
+//    (rho, g) sits at slot (rho, g) XOR F, F being the lane's final item,
+//    by loading query g XOR F_g into query slot g and row rho XOR F_rho
+//    into row slot rho. Every lane (every 2^k-th when 2 QG < 16) ends with
+//    the distance of one (row, query) and stores or appends it.
 // ---------------------------------------------------------------------------
 constexpr int kBulkRows = 8;
 constexpr int kBulkStages = 3;
@@ -416,38 +422,14 @@ struct L2Bulk {
   unsigned int* err;
 };
 
-// Sum over the 16 lanes of a half-warp of v[g] (g < QG): the lane's result
-// is the sum for query *g, which it returns.
-template <int QG>
-__device__ __forceinline__ float half_warp_reduce(float (&v)[QG], int lane,
-                                                  int* g) {
-  int base = 0;
-  int cnt = QG;
-#pragma unroll
-  for (int m = 8; m >= 1; m >>= 1) {
-    if (cnt >= 2) {
-      const int h = cnt / 2;
-      const bool up = (lane & m) != 0;
-#pragma unroll
-      for (int i = 0; i < h; ++i) {
-        const float send = up ? v[i] : v[i + h];
-        const float keep = up ? v[i + h] : v[i];
-        v[i] = keep + __shfl_xor_sync(kFull, send, m);
-      }
-      if (up) base += h;
-      cnt = h;
-    } else {
-      v[0] += __shfl_xor_sync(kFull, v[0], m);
-    }
-  }
-  *g = base;
-  return v[0];
-}
-
 template <int QG, int NC>
 __global__ void __launch_bounds__(kThreads, 2)
     l2_bulk_kernel(L2Bulk b, Level L) {
   extern __shared__ __align__(128) unsigned char smem_b[];
+  constexpr int V = 2 * QG;                        // values a lane starts with
+  constexpr int kLogV = V >= 16 ? 4 : V == 8 ? 3 : V == 4 ? 2 : 1;
+  constexpr int kDupShift = 4 - kLogV;             // lanes sharing a result
+  constexpr int kLogQG = kLogV - 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_groups = (L.n_queries + QG - 1) / QG;
   const int64_t group = blockIdx.x % n_groups;
@@ -478,36 +460,32 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   __syncwarp();
 
-  // Queries: chunk c, lane slice l16, as packed pairs.
+  // The lane's final item F = (rho_f, g_f) and its slot permutation.
   const int l16 = lane & 15, half = lane >> 4;
+  const int f_item = l16 >> kDupShift;
+  const int f_rho = f_item >> kLogQG, f_g = f_item & (QG - 1);
+  const bool owner = (l16 & ((1 << kDupShift) - 1)) == 0 &&
+                     q0 + f_g < L.n_queries;
+  const int64_t my_q = q0 + f_g;
+  const uint32_t my_bound =
+      (!store_all && owner) ? L.bound[my_q] : kNoBound;
+  // Query slot g holds query g ^ f_g: chunk c, lane slice l16, in pairs.
   uint64_t qp[QG][NC][2];
 #pragma unroll
-  for (int g = 0; g < QG; ++g)
+  for (int g = 0; g < QG; ++g) {
+    const int64_t qq = q0 + (g ^ f_g);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       float v[4] = {0.f, 0.f, 0.f, 0.f};
-      if (q0 + g < L.n_queries) {
-        const float* qs = b.queries + (q0 + g) * b.query_stride + 64 * c +
-                          4 * l16;
+      if (qq < L.n_queries) {
+        const float* qs = b.queries + qq * b.query_stride + 64 * c + 4 * l16;
 #pragma unroll
         for (int e = 0; e < 4; ++e) v[e] = __ldg(qs + e);
       }
       qp[g][c][0] = pk(v[0], v[1]);
       qp[g][c][1] = pk(v[2], v[3]);
     }
-  // This lane's query after the reduction, and which lanes own a result.
-  int my_g = 0;
-  {
-    float probe[QG];
-#pragma unroll
-    for (int g = 0; g < QG; ++g) probe[g] = 0.f;
-    half_warp_reduce<QG>(probe, lane, &my_g);
   }
-  constexpr int kDupMask = QG >= 8 ? 1 : QG == 4 ? 3 : QG == 2 ? 7 : 15;
-  const bool owner = (lane & kDupMask) == 0 && q0 + my_g < L.n_queries;
-  const int64_t my_q = q0 + my_g;
-  const uint32_t my_bound =
-      (!store_all && owner) ? L.bound[my_q] : kNoBound;
 
   // The warp's batches: in tile t, scan indices [t * tile + warp * run,
   // + run) in batches of 8; they stay below m for a prefix of the sequence.
@@ -543,37 +521,49 @@ __global__ void __launch_bounds__(kThreads, 2)
       break;
     }
     const int64_t j0 = batch_j0(u);
-    const float* sb = wbuf + size_t(st) * kBulkRows * b.row_stride;
+    const float* sb = wbuf + size_t(st) * kBulkRows * b.row_stride + 4 * l16;
 #pragma unroll 1
-    for (int step = 0; step < kBulkRows / 2; ++step) {
-      const int r = 2 * step + half;
-      const float* row = sb + r * b.row_stride + 4 * l16;
-      uint64_t acc[QG];
+    for (int step = 0; step < kBulkRows / 4; ++step) {
+      float v[V];
 #pragma unroll
-      for (int g = 0; g < QG; ++g) acc[g] = 0;
+      for (int rho = 0; rho < 2; ++rho) {
+        // Row slot rho holds row 2 (rho ^ f_rho) + half of the step.
+        const float* row = sb + (4 * step + 2 * (rho ^ f_rho) + half) *
+                                    b.row_stride;
+        uint64_t acc[QG];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        const float4 rv = *reinterpret_cast<const float4*>(row + 64 * c);
-        const uint64_t r01 = pk(rv.x, rv.y), r23 = pk(rv.z, rv.w);
+        for (int g = 0; g < QG; ++g) acc[g] = 0;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const float4 rv = *reinterpret_cast<const float4*>(row + 64 * c);
+          const uint64_t r01 = pk(rv.x, rv.y), r23 = pk(rv.z, rv.w);
+#pragma unroll
+          for (int g = 0; g < QG; ++g) {
+            const uint64_t d01 = sub2(qp[g][c][0], r01);
+            const uint64_t d23 = sub2(qp[g][c][1], r23);
+            acc[g] = fma2(d01, d01, acc[g]);
+            acc[g] = fma2(d23, d23, acc[g]);
+          }
+        }
 #pragma unroll
         for (int g = 0; g < QG; ++g) {
-          const uint64_t d01 = sub2(qp[g][c][0], r01);
-          const uint64_t d23 = sub2(qp[g][c][1], r23);
-          acc[g] = fma2(d01, d01, acc[g]);
-          acc[g] = fma2(d23, d23, acc[g]);
+          const float2 a2 = upk(acc[g]);
+          v[rho * QG + g] = a2.x + a2.y;
         }
       }
-      float part[QG];
+      // The butterfly: keep the first half, add the partner's second.
+      int cnt = V;
 #pragma unroll
-      for (int g = 0; g < QG; ++g) {
-        const float2 a2 = upk(acc[g]);
-        part[g] = a2.x + a2.y;
+      for (int mm = 8; mm >= 1; mm >>= 1) {
+        const int h = cnt >= 2 ? cnt / 2 : 1;
+#pragma unroll
+        for (int i = 0; i < h; ++i)
+          v[i] += __shfl_xor_sync(kFull, v[cnt >= 2 ? i + h : i], mm);
+        cnt = h;
       }
-      int gq;
-      const float dist = half_warp_reduce<QG>(part, lane, &gq);
-      const int64_t j = j0 + r;
+      const int64_t j = j0 + 4 * step + 2 * f_rho + half;
       if (!owner || j >= m) continue;
-      const uint32_t key = dist_key(dist);
+      const uint32_t key = dist_key(v[0]);
       const uint32_t node =
           uint32_t(every ? j : (j >> 5) * spacing + (j & 31));
       uint32_t* qk = L.keys + my_q * L.cap;
@@ -757,11 +747,13 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
   }
 
   // First one histogram of the keys' offsets from their smallest, in 2,048
-  // bins spanning their range: when the entries before the end of the bin
-  // holding the need-th fit the sort buffer, those are gathered (ranged).
+  // bins spanning their range. A bound needs no more: the last key of the
+  // bin holding the need-th has at least need keys at or under it. A result
+  // gathers the entries before that bin's end when they fit the sort buffer
+  // (ranged).
   bool ranged = false;
   uint64_t range_end = 0;  // ranged: the keys under it are gathered
-  if (n > kSortMax) {
+  if (n > kSortMax || a.mode != kFinal) {
     uint32_t lo = kNoBound, hi = 0u;
 #pragma unroll 4
     for (int64_t i = tid; i < n; i += kSelThreads) {
@@ -789,6 +781,15 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
     __syncthreads();
     ranged = pick[1] + pick[2] <= uint32_t(kSortMax);
     range_end = uint64_t(lo) + (uint64_t(pick[0] + 1) << shift);
+    if (a.mode != kFinal) {
+      if (tid == 0) {
+        const uint32_t b = range_end - 1 > uint64_t(kNoBound)
+                               ? kNoBound
+                               : uint32_t(range_end - 1);
+        a.bound[q] = a.mode == kFirstBound ? b : umin(a.bound[q], b);
+      }
+      return;
+    }
     __syncthreads();  // pick is rewritten below
   }
 
