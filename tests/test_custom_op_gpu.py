@@ -74,3 +74,36 @@ def test_runs_on_a_non_default_stream_and_device_guard():
         *(t.float().cpu().numpy() for t in args))
     helpers.assert_close(out.double().cpu().numpy(), want, 1e-2,
                          8e-3 * float(args[2].float().abs().max()))
+
+
+def _projection_views(dtype=torch.bfloat16, B=3, N=11, H=4, D=32):
+    """q, k, v as head-split views of one [B, N, 3 H D] projection (tokens
+    outer to heads), like the compiled model's."""
+    gen = torch.Generator().manual_seed(1)
+    qkv = torch.randn(B, N, 3, H, D, generator=gen).to('cuda', dtype)
+    q, k, v = qkv.permute(2, 0, 3, 1, 4)
+    scale = torch.full((1, H, 1, 1), 0.05, device='cuda')
+    return q, k, v, scale
+
+
+@pytest.mark.parametrize('kernel', ['auto', 'generic', 'small'])
+def test_output_follows_the_projection_layout(kernel):
+    from vectra_b200 import custom_ops  # pylint: disable=import-outside-toplevel
+    q, k, v, scale = _projection_views()
+    out = custom_ops.rbf_attention_with_kernel(q, k, v, scale, None, kernel)
+    assert out.stride() == custom_ops.output_strides(q, v.shape[-1])
+    assert out.transpose(1, 2).is_contiguous()  # the model's reshape: a view
+    want = rbf_oracle.expanded_rbf_attention(
+        *(t.float().cpu().numpy() for t in (q, k, v, scale)), None)
+    helpers.assert_close(out.double().cpu().numpy(), want, 2e-2, 2e-2)
+    contiguous = custom_ops.rbf_attention_with_kernel(
+        q.contiguous(), k.contiguous(), v.contiguous(), scale, None, kernel)
+    assert contiguous.is_contiguous()
+    assert torch.equal(out, contiguous)  # same values, other layout
+
+
+def test_opcheck_projection_views():
+    torch.library.opcheck(
+        torch.ops.vectra.rbf_attention.default, _projection_views(),
+        test_utils=('test_schema', 'test_faketensor',
+                    'test_aot_dispatch_static', 'test_aot_dispatch_dynamic'))

@@ -91,8 +91,21 @@ at::Tensor run(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
   if (key_bias.has_value() && key_bias->defined())
     bias = side_input(*key_bias, q);
 
-  at::Tensor out = at::empty({q.size(0), q.size(1), q.size(2), v.size(3)},
-                             v.options());
+  // The output follows q's order of heads and tokens: when q's tokens are
+  // outer to its heads (a head-split view of a [B, N, H * D] projection),
+  // out is a head-transposed view of [B, Nq, H, Dv] memory, as PyTorch's
+  // attention kernels return, so out.transpose(1, 2).reshape(B, Nq, H * Dv)
+  // needs no copy; otherwise out is contiguous [B, H, Nq, Dv]. The fake
+  // implementation (vectra_b200/custom_ops.py) applies the same rule.
+  const bool tokens_outer =
+      q.size(1) > 1 && q.size(2) > 1 && q.stride(2) > q.stride(1);
+  at::Tensor out =
+      tokens_outer
+          ? at::empty({q.size(0), q.size(2), q.size(1), v.size(3)},
+                      v.options())
+                .permute({0, 2, 1, 3})
+          : at::empty({q.size(0), q.size(1), q.size(2), v.size(3)},
+                      v.options());
   vectra_rbf_args a{};
   a.q = describe(q);
   a.k = describe(k);

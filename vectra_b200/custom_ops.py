@@ -13,6 +13,13 @@ through libvectra_rbf.so. Differences from the reference, on purpose:
   raises NotImplementedError for CPU tensors. The reference's CPU
   arithmetic (reference.matmul_rbf_attention) is the oracle here, not
   product code.
+* The output's layout follows q (`output_strides`): when q's tokens are
+  outer to its heads (q a head-split view of a [B, N, H * D] projection,
+  as in the compiled model), the output is a head-transposed view of
+  [B, Nq, H, Dv] memory, as PyTorch's own attention kernels return, so the
+  model's `.transpose(1, 2).reshape(B, N, H * Dv)` is a view instead of a
+  copy; otherwise it is contiguous, as the reference's is. Values are the
+  same either way.
 
 Typical usage (unchanged):
 
@@ -28,16 +35,34 @@ OP_NAME = 'vectra::rbf_attention'
 torch.ops.load_library(_lib.TORCH_EXT_PATH)
 
 
+def output_strides(q, dv: int) -> tuple:
+    """Strides of the operator's [B, H, Nq, Dv] output for query q: those of
+    a head-transposed view of [B, Nq, H, Dv] memory when q's tokens are
+    outer to its heads (H > 1, Nq > 1, q.stride(2) > q.stride(1)), else
+    contiguous. The CUDA implementation allocates the same way
+    (csrc/torch_ext.cpp)."""
+    b, h, n = q.shape[0], q.shape[1], q.shape[2]
+    if h > 1 and n > 1 and q.stride(2) > q.stride(1):
+        return (n * h * dv, dv, h * dv, 1)
+    return (h * n * dv, n * dv, dv, 1)
+
+
+def _empty_output(q, v):
+    dv = v.shape[-1]
+    return q.new_empty_strided((*q.shape[:-1], dv), output_strides(q, dv),
+                               dtype=v.dtype)
+
+
 @torch.library.register_fake(OP_NAME)
 def _rbf_attention_fake(q, k, v, scale, key_bias=None):
-    del k, scale, key_bias  # Only the output shape matters while tracing.
-    return q.new_empty((*q.shape[:-1], v.shape[-1]), dtype=v.dtype)
+    del k, scale, key_bias  # Only the output's shape and layout matter here.
+    return _empty_output(q, v)
 
 
 @torch.library.register_fake('vectra_b200::rbf_attention_with_flags')
 def _rbf_attention_with_flags_fake(q, k, v, scale, key_bias, flags):
     del k, scale, key_bias, flags
-    return q.new_empty((*q.shape[:-1], v.shape[-1]), dtype=v.dtype)
+    return _empty_output(q, v)
 
 
 def cuda_available() -> bool:
@@ -60,7 +85,8 @@ def rbf_attention(q, k, v, scale, key_bias=None) -> torch.Tensor:
         and -inf for padding.
 
     Returns:
-      [B, H, Nq, Dv] in v's dtype. Rows whose keys are all masked are NaN.
+      [B, H, Nq, Dv] in v's dtype, laid out as `output_strides` says. Rows
+      whose keys are all masked are NaN.
 
     Raises:
       ValueError: bad ranks, shapes or dtypes, or a key_bias that varies
@@ -112,8 +138,7 @@ def kernel_for(q, k, v, scale, key_bias=None, kernel: str = 'auto') -> str:
     a.q, a.k, a.v = _describe(q), _describe(k), _describe(v)
     a.scale, a.key_bias = _describe(scale), _describe(key_bias)
     a.out = 0x10000
-    dv = v.shape[-1]
-    st = [q.shape[1] * q.shape[2] * dv, q.shape[2] * dv, dv, 1]
+    st = output_strides(q, v.shape[-1])
     for i in range(4):
         a.out_stride[i] = st[i]
     a.flags = 0 if kernel == 'auto' else KERNELS[kernel]
