@@ -1018,8 +1018,7 @@ def run_scan(args):
         call = _lib.LIB.vectra_scan_pq_topk
     stream = torch.cuda.current_stream(dev)
     handle = ctypes.c_void_p(stream.cuda_stream)
-    # Sample pass, its bounds, the main pass and the merge when the shard
-    # spans several 4,096-candidate tiles.
+    # A level kernel and a select per level, then the re-scan check.
     launches_per_step = scan_launches(data.shape[0], SCAN_K)
 
     def step(i):

@@ -18,7 +18,10 @@
  *
  * Every call is asynchronous on the given CUDA stream; pointers are device
  * pointers; the caller owns every buffer, including a workspace sized by
- * vectra_scan_workspace_bytes. Status codes are those of vectra_rbf.h.
+ * vectra_scan_workspace_bytes. Status codes are those of vectra_rbf.h. The
+ * kernels' waits on their own copies are bounded: one that runs out sets a
+ * bit of the device error word that vectra_rbf_check_device_errors reports,
+ * and the kernel returns.
  */
 #ifndef VECTRA_SCAN_H_
 #define VECTRA_SCAN_H_
