@@ -661,7 +661,7 @@ __device__ __forceinline__ void smem_bitonic(unsigned long long* v,
     for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
 #pragma unroll 1
       for (uint32_t i = t; i < p2 / 2; i += nt) {
-        const uint32_t lo = (i / stride) * 2 * stride + (i % stride);
+        const uint32_t lo = 2 * i - (i & (stride - 1));  // stride: 2^m
         const uint32_t hi = lo + stride;
         const bool up = (lo & size) == 0;
         const unsigned long long x = v[lo], y = v[hi];
