@@ -117,14 +117,17 @@ def peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 'fallback'
 
 
-def ncu_traffic(config):
-    """DRAM bytes per launch from the committed ncu summary, if any."""
-    kernel = {4: 'rbf_tc', 5: 'rbf_small'}.get(config, 'rbf_decode')
-    path = os.path.join(ROOT, 'profiles', f'{kernel}_config{config}.txt')
+def ncu_traffic(config, name=None, key='dram_bytes_per_launch_full'):
+    """DRAM bytes per launch from the committed ncu summary, if any
+    (profiles/<kernel>_config<config>.txt, or profiles/<name>.txt)."""
+    if name is None:
+        kernel = {4: 'rbf_tc', 5: 'rbf_small'}.get(config, 'rbf_decode')
+        name = f'{kernel}_config{config}'
+    path = os.path.join(ROOT, 'profiles', f'{name}.txt')
     try:
         with open(path, encoding='utf-8') as f:
             for line in f:
-                m = re.match(r'dram_bytes_per_launch_full:\s*([0-9.eE+]+)',
+                m = re.match(re.escape(key) + r':\s*([0-9.eE+]+)',
                              line.strip())
                 if m:
                     return float(m.group(1))
@@ -1112,7 +1115,9 @@ def run_scan(args):
             'gpu_launches': launches_per_step * args.steps,
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
                          'unit': 'GB/s', 'frac': achieved / hbm,
-                         'traffic': None,
+                         'traffic': ncu_traffic(
+                             None, 'scan_levels',
+                             f'dram_bytes_full_level_{args.scan}'),
                          'peak_kind': f'HBM copy, {peak_kind}',
                          'algorithmic_bytes_per_launch': alg_bytes,
                          'kernel': 'every launch of a step (sample and '
