@@ -317,3 +317,20 @@ def test_l2_bulk_copy_row_stride_and_tail():
             queries[qi].cpu().numpy(), rows.cpu().numpy(), 33)
         _check_l2(gd[qi].cpu().numpy(), gn[qi].cpu().numpy(), 33, wd, wn,
                   queries[qi].cpu().numpy(), rows.cpu().numpy(), 128)
+
+
+def test_l2_rows_with_a_large_common_offset():
+    # Coordinates near 1,000 (e.g. unnormalised features): q_d - r_d of
+    # nearby float32 values is exact, so direct differences keep the
+    # reference's tolerance where ||q||^2 + ||r||^2 - 2 q.r would lose it.
+    rng = np.random.default_rng(27)
+    n, d = 60000, 128
+    rows = (1000.0 + rng.standard_normal((n, d))).astype(np.float32)
+    queries = (rows[rng.integers(0, n, 4)] +
+               0.05 * rng.standard_normal((4, d))).astype(np.float32)
+    gd, gn, gc = scan.l2_topk(torch.from_numpy(queries).cuda(),
+                              torch.from_numpy(rows).cuda(), 32)
+    gd, gn = gd.cpu().numpy(), gn.cpu().numpy()
+    for qi in range(4):
+        wd, wn = scan_oracle.exhaustive_l2_topk(queries[qi], rows, 32)
+        _check_l2(gd[qi], gn[qi], 32, wd, wn, queries[qi], rows, d)
