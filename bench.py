@@ -925,7 +925,8 @@ def scan_launches(n_cand, k):
         return 2
     levels, s = 1, sample0
     while levels < 6 and k * n_cand > (cap // 4) * s:
-        s2 = s * (cap // 8) // k
+        enough = -(-k * n_cand // (cap // 4))
+        s2 = -(-min(enough, s * (cap // 8) // k) // 32) * 32
         if 2 * s2 >= n_cand:
             break
         levels += 1

@@ -1276,9 +1276,12 @@ Plan plan_for(int64_t n_cand, int k) {
   p.groups[p.n_levels++] = s / 32;
   // A level's bound is about the (k / s) quantile: the next level admits
   // about k * (its size) / s candidates. Go to every candidate once that is
-  // at most a quarter of the buffer, else sample enough for an eighth.
+  // at most a quarter of the buffer; else sample just enough for that (at
+  // most what keeps this level's admissions to an eighth of the buffer).
   while (p.n_levels < 6 && int64_t(k) * n_cand > (kCap / 4) * s) {
-    const int64_t s2 = s * (kCap / 8) / k;
+    const int64_t enough = (int64_t(k) * n_cand + kCap / 4 - 1) / (kCap / 4);
+    const int64_t most = s * (kCap / 8) / k;
+    const int64_t s2 = (std::min(enough, most) + 31) / 32 * 32;
     if (2 * s2 >= n_cand) break;
     p.groups[p.n_levels++] = s2 / 32;
     s = s2;
