@@ -648,6 +648,41 @@ __device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t* wtot,
   return r;
 }
 
+// Bitonic sort, ascending, of 32 << LOG_PER values held by one warp in
+// registers: element e = j * 32 + lane in v[j]. Strides under 32 pair lanes
+// (shuffles), larger ones a lane's own registers.
+template <int LOG_PER>
+__device__ __forceinline__ void warp_bitonic(
+    unsigned long long (&v)[1 << LOG_PER], int lane) {
+  constexpr int PER = 1 << LOG_PER;
+#pragma unroll
+  for (int ls = 1; ls <= 5 + LOG_PER; ++ls) {
+    const int size = 1 << ls;
+#pragma unroll
+    for (int lt = ls - 1; lt >= 0; --lt) {
+      const int stride = 1 << lt;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const bool up = ((j * 32 + lane) & size) == 0;
+        if (stride >= 32) {
+          const int js = stride >> 5;
+          if (j & js) continue;
+          const unsigned long long x = v[j], y = v[j | js];
+          if ((x > y) == up) {
+            v[j] = y;
+            v[j | js] = x;
+          }
+        } else {
+          const unsigned long long o = __shfl_xor_sync(kFull, v[j], stride);
+          const bool keep_min = ((lane & stride) == 0) == up;
+          const bool less = v[j] < o;
+          v[j] = keep_min ? (less ? v[j] : o) : (less ? o : v[j]);
+        }
+      }
+    }
+  }
+}
+
 // Bitonic sort, ascending, of p2 (a power of two) values in shared memory
 // by threads t = 0 .. nt - 1: one warp (WARP, __syncwarp between stages) or
 // the whole block (__syncthreads).
@@ -715,8 +750,14 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
   const int64_t n = int64_t(n_total) < a.cap ? int64_t(n_total) : a.cap;
   const uint32_t* qk = a.keys + q * a.cap;
   const uint32_t* qn = a.nodes + q * a.cap;
-#pragma unroll 4
-  for (int64_t i = tid; i < n; i += kSelThreads) skey[i] = qk[i];
+  uint32_t lo = kNoBound, hi = 0u;  // the keys' range, kept while staging
+#pragma unroll 16
+  for (int64_t i = tid; i < n; i += kSelThreads) {
+    const uint32_t kv = qk[i];
+    skey[i] = kv;
+    lo = umin(lo, kv);
+    hi = umax(hi, kv);
+  }
   hist[tid] = 0u;
   hist[tid + kSelThreads] = 0u;
   if (tid == 0) n_sel_sh = 0u;
@@ -754,12 +795,6 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
   bool ranged = false;
   uint64_t range_end = 0;  // ranged: the keys under it are gathered
   if (n > kSortMax || a.mode != kFinal) {
-    uint32_t lo = kNoBound, hi = 0u;
-#pragma unroll 4
-    for (int64_t i = tid; i < n; i += kSelThreads) {
-      lo = umin(lo, skey[i]);
-      hi = umax(hi, skey[i]);
-    }
     lo = __reduce_min_sync(kFull, lo);
     hi = __reduce_max_sync(kFull, hi);
     if (lane == 0) {
@@ -885,7 +920,19 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(Select a) {
                                                        : uint32_t(kSortMax);
   uint32_t p2 = 2;
   while (p2 < n_sel) p2 <<= 1;
-  if (p2 <= 256u) {  // one warp sorts
+  if (p2 <= 128u) {  // one warp sorts in registers
+    if (warp == 0) {
+      unsigned long long v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t e = uint32_t(j * 32 + lane);
+        v[j] = e < n_sel ? sorted[e] : ~0ull;
+      }
+      warp_bitonic<2>(v, lane);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sorted[j * 32 + lane] = v[j];
+    }
+  } else if (p2 <= 256u) {  // one warp sorts in shared memory
     if (warp == 0) {
       for (uint32_t i = n_sel + lane; i < p2; i += 32) sorted[i] = ~0ull;
       __syncwarp();
