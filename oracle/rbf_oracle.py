@@ -150,7 +150,7 @@ def eager_rbf_attention(q, k, v, scale, key_bias=None,
     (`eager_rbf_attention`): it materialises the [B,H,Nq,Nk,D] difference
     tensor, so it is only used at sizes where that fits comfortably. It is
     computed in `dtype` (float32 by default: the fp32 reference that bf16
-    results are judged against).
+    results are compared against).
     """
     qd, kd, vd = (np.asarray(t, dtype=dtype) for t in (q, k, v))
     diff = qd[..., :, None, :] - kd[..., None, :, :]
@@ -232,7 +232,7 @@ def tiled_rbf_attention(q, k, v, scale, key_bias=None, block_q=64,
 # ---------------------------------------------------------------------------
 
 def reference_output(q, k, v, scale, key_bias=None, out_dtype='f32'):
-    """The fp32 reference the CUDA path is judged against.
+    """The fp32 reference the CUDA path is compared against.
 
     The eager formulation (reference.py:46-58) in float32 on the (already
     rounded) inputs, rounded to the output dtype the operator returns
