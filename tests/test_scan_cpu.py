@@ -135,3 +135,23 @@ def test_null_and_shape_errors_need_no_gpu():
     assert _lib.LIB.vectra_scan_pq_topk(p, None) == _lib.ERR_SHAPE
     assert _lib.LIB.vectra_pq_distance_tables(
         0x10000, 1, 8, 0x10000, 8, 3, 0x10000, None) == _lib.ERR_SHAPE
+
+
+def test_level_plan_launch_counts():
+    # bench.py's count of a scan call's launches (a level kernel and a
+    # select per level, plus the two of the overflow re-scan): one level up
+    # to 32,768 candidates, two for the L2 bench (1 M rows, k = 64), three
+    # for the PQ bench (16 M codes) and for k = 256 over 1 M rows.
+    import bench  # pylint: disable=import-outside-toplevel
+    assert bench.scan_launches(1000, 64) == 2
+    assert bench.scan_launches(32768, 256) == 2
+    assert bench.scan_launches(1 << 20, 64) == 6
+    assert bench.scan_launches(1 << 24, 64) == 8
+    assert bench.scan_launches(1 << 20, 256) == 8
+
+
+def test_static_scratch_covers_the_bench_scan():
+    # vectra_scan_l2_topk_noalloc serves the L2 bench's shape (8 queries
+    # over 1 M rows, k = 64) from its 8 MB static scratch.
+    assert 0 < scan.workspace_bytes(8, 1 << 20, 64) <= \
+        scan.NOALLOC_SCRATCH_BYTES
