@@ -5,9 +5,10 @@
 // ProductQuantizer::ComputeDistanceTable (engine/src/index/pq_codec.cc).
 //
 // Design (B200): score every candidate once at HBM speed, keep almost none.
-//  * Distances: a lane per candidate row, QG queries per CTA (their vectors
-//    or PQ tables in shared memory). L2 sums (q_d - r_d)^2 in float32 with
-//    packed f32x2 subtract/FMA from 16-byte row loads; PQ sums table entries
+//  * Distances: QG queries per CTA, a lane per candidate row (PQ tables or
+//    query vectors in shared memory), or for L2 over every row 16 lanes per
+//    row staged by bulk copy (l2_bulk_kernel below). L2 sums (q_d - r_d)^2
+//    in float32 with packed f32x2 subtract/FMA; PQ sums table entries
 //    in PqAdcDistance's order (four chains, (l0 + l1) + (l2 + l3), then the
 //    tail: bit-identical to the reference). A distance becomes a 32-bit key
 //    whose unsigned order is the float order, and (key, node) as one 64-bit
@@ -25,8 +26,10 @@
 //  * Select: one CTA of 1,024 threads per query stages the buffer's keys in
 //    shared memory; one histogram over their range (2,048 bins) usually
 //    leaves few enough entries at or under the bin of the k-th to sort
-//    (bitonic, in one warp up to 256); otherwise a radix select over 11-bit
-//    digits of (key, node) narrows them first.
+//    (bitonic: one warp in registers up to 128 entries, in shared memory up
+//    to 256, the block up to 2,048); otherwise a radix select over 11-bit
+//    digits of (key, node) narrows them first. A bound needs only the end
+//    of the k-th's bin.
 //  * A last level that admits more candidates than its buffer holds (mass
 //    ties at the bound) is redone for that query by the warp-list scan:
 //    per-warp sorted lists in registers fed by ballot-filtered insertion,
