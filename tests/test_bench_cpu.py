@@ -70,3 +70,33 @@ def test_model_reference_arm_prints_one_json_line(capfd, monkeypatch):
     assert line['impl'] == 'reference' and line['unit'] == 'predictions/s'
     assert line['value'] > 0 and line['cpu_baseline']['cores'] >= 1
     assert line['e2e']['h2d_bytes_per_step'] == 0
+
+
+@pytest.mark.parametrize('kind', ['l2', 'pq'])
+def test_scan_reference_arm_prints_one_json_line(capfd, monkeypatch, kind):
+    monkeypatch.delenv('RANK', raising=False)
+    # A small shard and short timing windows: the arm's contract, not its
+    # number.
+    monkeypatch.setattr(bench, 'SCAN_L2', dict(rows=1 << 14, dim=32))
+    monkeypatch.setattr(bench, 'SCAN_PQ', dict(rows=1 << 15, subspaces=8))
+    timed = bench.time_scan_cpu
+    monkeypatch.setattr(
+        bench, 'time_scan_cpu',
+        lambda k, d, q, seconds, threads: timed(k, d, q, 0.05, threads))
+    assert bench.main(['--impl', 'reference', '--scan', kind, '--steps', '1',
+                       '--warmup', '0']) == 0
+    out = capfd.readouterr().out.strip().splitlines()
+    assert len(out) == 1, out
+    line = json.loads(out[0])
+    assert line['impl'] == 'reference'
+    assert (line['metric'], line['unit']) == bench.scan_metric(kind)
+    assert line['value'] > 0 and line['cpu_baseline']['cores'] >= 1
+    assert line['cpu_baseline']['kind'] in ('reference', 'port')
+    assert line['e2e']['h2d_bytes_per_step'] == 0
+
+
+def test_scan_traffic_comes_from_the_committed_profile():
+    traffic = bench.ncu_traffic(None, 'scan_levels',
+                                'dram_bytes_full_level_l2')
+    rows = bench.SCAN_L2['rows'] * bench.SCAN_L2['dim'] * 4
+    assert traffic is not None and rows <= traffic < 1.1 * rows
