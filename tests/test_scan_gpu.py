@@ -319,6 +319,28 @@ def test_l2_bulk_copy_row_stride_and_tail():
                   queries[qi].cpu().numpy(), rows.cpu().numpy(), 128)
 
 
+def test_l2_bulk_copy_suffix_column_view():
+    # rows = base[:, 64:] of an [N, 128] tensor: stride 128, dimension 64,
+    # and the last row's final element is the storage's last element. A
+    # batch copy ends at its last row's final element, never a full stride
+    # past it.
+    rng = np.random.default_rng(31)
+    n = 40003
+    base = torch.from_numpy(rng.standard_normal((n, 128)).astype(
+        np.float32)).cuda()
+    rows = base[:, 64:]
+    assert (rows.storage_offset() + (n - 1) * rows.stride(0) + 64 ==
+            base.untyped_storage().nbytes() // 4)
+    queries = (base[[5, 17, 30001], 64:] + 0.03).contiguous()
+    gd, gn, _ = scan.l2_topk(queries, rows, 24)
+    host_rows = rows.cpu().numpy()
+    for qi in range(3):
+        q = queries[qi].cpu().numpy()
+        wd, wn = scan_oracle.exhaustive_l2_topk(q, host_rows, 24)
+        _check_l2(gd[qi].cpu().numpy(), gn[qi].cpu().numpy(), 24, wd, wn,
+                  q, host_rows, 64)
+
+
 def test_l2_rows_with_a_large_common_offset():
     # Coordinates near 1,000 (e.g. unnormalised features): q_d - r_d of
     # nearby float32 values is exact, so direct differences keep the

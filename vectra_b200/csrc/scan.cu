@@ -504,7 +504,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int64_t nv = m - j0 < kBulkRows ? m - j0 : kBulkRows;
     const int64_t i0 = every ? j0 : (j0 >> 5) * spacing + (j0 & 31);
     const int st = int(u % kBulkStages);
-    const uint32_t bytes = uint32_t(nv * b.row_stride * sizeof(float));
+    // The batch's rows from the first one's start to the last one's final
+    // element (64 * NC floats): a row view that ends where its storage ends
+    // (a suffix of each row's columns) is never read past. Both terms are
+    // multiples of 16 bytes, as the bulk copy requires.
+    const uint32_t bytes =
+        uint32_t(((nv - 1) * b.row_stride + 64 * NC) * sizeof(float));
     mbar_arrive_expect_tx(bar0 + 8 * st, bytes);
     bulk_g2s(smem_addr(wbuf + size_t(st) * kBulkRows * b.row_stride),
              b.rows + i0 * b.row_stride, bytes, bar0 + 8 * st, policy);
