@@ -113,10 +113,20 @@ def test_bad_shapes_raise_value_error():
                                                       device='cuda'))
 
 
-def test_cpu_tensors_are_not_silently_computed():
+def test_dispatch_by_device_never_crosses_it():
+    # CPU tensors run the CPU implementation (no kernel launch); CUDA
+    # tensors always launch this library's kernel; mixed devices raise.
     q = torch.randn(1, 1, 2, 8)
-    with pytest.raises(NotImplementedError):
-        torch.ops.vectra.rbf_attention(q, q, q, torch.tensor(0.1))
+    before = vectra_b200.launch_count()
+    out = torch.ops.vectra.rbf_attention(q, q, q, torch.tensor(0.1))
+    assert out.device.type == 'cpu' and vectra_b200.launch_count() == before
+    qc = q.cuda()
+    got = torch.ops.vectra.rbf_attention(qc, qc, qc, torch.tensor(0.1))
+    torch.cuda.synchronize()
+    assert vectra_b200.launch_count() == before + 1
+    torch.testing.assert_close(got.cpu(), out, rtol=1e-5, atol=1e-6)
+    with pytest.raises((ValueError, RuntimeError)):
+        torch.ops.vectra.rbf_attention(qc, q, qc, torch.tensor(0.1))
 
 
 def test_forced_kernel_that_cannot_run_raises():

@@ -31,9 +31,8 @@ BUILD = os.path.join(PKG, '_build')
 LIB = os.path.join(PKG, 'libvectra_rbf.so')
 TORCH_EXT = os.path.join(PKG, '_vectra_rbf_torch.so')
 
-CU_SOURCES = ['capi.cu', 'rbf_generic.cu', 'rbf_decode.cu',
-              'rbf_decode_mma.cu', 'rbf_tc.cu', 'rbf_small.cu',
-              'tma_maps.cu', 'scan.cu']
+CU_SOURCES = ['capi.cu', 'rbf_generic.cu', 'rbf_decode.cu', 'rbf_tc.cu',
+              'rbf_small.cu', 'tma_maps.cu', 'scan.cu']
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 
@@ -121,26 +120,36 @@ def build_library(force=False, verbose=False, extra_flags=(), lib_path=LIB,
 
 
 def build_torch_extension(force=False, verbose=False):
-    """Compiles the PyTorch binding against the installed torch."""
+    """Compiles the PyTorch binding against the installed torch: the
+    operator's registration and CUDA launcher (torch_ext.cpp) and its CPU
+    implementation (rbf_cpu.cpp, parallel over planes with ATen's OpenMP
+    thread pool, so it is compiled with -fopenmp and linked against the
+    libgomp that torch itself loads)."""
     import torch  # pylint: disable=import-outside-toplevel
     from torch.utils import cpp_extension  # pylint: disable=import-outside-toplevel
 
     src = os.path.join(CSRC, 'torch_ext.cpp')
-    if not (force or _stale(TORCH_EXT, [src, LIB] + _headers())):
+    cpu_src = os.path.join(CSRC, 'rbf_cpu.cpp')
+    if not (force or _stale(TORCH_EXT, [src, cpu_src, LIB] + _headers())):
         return TORCH_EXT
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)  # pylint: disable=protected-access
     includes = cpp_extension.include_paths(device_type='cuda')
-    cmd = ['g++', '-shared', '-fPIC', '-O2', '-std=c++17',
-           f'-D_GLIBCXX_USE_CXX11_ABI={abi}', '-DTORCH_API_INCLUDE_EXTENSION_H',
-           '-DTORCH_EXTENSION_NAME=_vectra_rbf_torch', '-I', INCLUDE,
-           '-I', os.path.join(cuda_home(), 'include')]
+    common = ['-fPIC', '-std=c++17', f'-D_GLIBCXX_USE_CXX11_ABI={abi}',
+              '-DTORCH_API_INCLUDE_EXTENSION_H',
+              '-DTORCH_EXTENSION_NAME=_vectra_rbf_torch', '-I', INCLUDE,
+              '-I', os.path.join(cuda_home(), 'include')]
     for inc in includes:
-        cmd += ['-isystem', inc]
-    cmd += [src, '-o', TORCH_EXT, '-L', PKG, '-lvectra_rbf']
+        common += ['-isystem', inc]
+    os.makedirs(BUILD, exist_ok=True)
+    cpu_obj = os.path.join(BUILD, 'rbf_cpu.o')
+    _run(['g++', '-c', '-O3', '-fopenmp'] + common + [cpu_src, '-o', cpu_obj],
+         verbose)
+    cmd = ['g++', '-shared', '-O2'] + common + [src, cpu_obj, '-o', TORCH_EXT,
+                                                '-L', PKG, '-lvectra_rbf']
     for libdir in cpp_extension.library_paths(device_type='cuda'):
         cmd += ['-L', libdir]
     cmd += ['-lc10', '-lc10_cuda', '-ltorch', '-ltorch_cpu', '-ltorch_cuda',
-            '-Wl,-rpath,$ORIGIN']
+            '-l:libgomp.so.1', '-Wl,-rpath,$ORIGIN']
     _run(cmd, verbose)
     return TORCH_EXT
 

@@ -7,17 +7,28 @@
 // kernels/vectra_kernels/custom_ops.py:52-72). The CUDA implementation
 // replaces _rbf_attention_cuda (custom_ops.py:75-85): it validates, reads
 // strides, allocates the output and calls the C ABI of libvectra_rbf.so on
-// the current stream. There is no CPU kernel: calling the operator on CPU
-// tensors raises (the CUDA path never falls back to the CPU). The fake
-// (meta) implementation lives in vectra_b200/custom_ops.py.
+// the current stream. CPU tensors dispatch to this library's CPU
+// implementation (rbf_cpu.cpp), the counterpart of the reference's default
+// implementation; CUDA tensors always reach the CUDA kernels and never fall
+// back to the CPU. The fake (meta) implementation lives in
+// vectra_b200/custom_ops.py.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
 #include <optional>
+#include <vector>
 
 #include "vectra_rbf.h"
+
+namespace vectra_cpu {
+at::Tensor rbf_attention_cpu(const at::Tensor& q, const at::Tensor& k,
+                             const at::Tensor& v, const at::Tensor& scale,
+                             const std::optional<at::Tensor>& key_bias,
+                             at::IntArrayRef out_sizes,
+                             at::IntArrayRef out_strides);
+}  // namespace vectra_cpu
 
 namespace {
 
@@ -73,6 +84,28 @@ at::Tensor side_input(const at::Tensor& t, const at::Tensor& q) {
   TORCH_CHECK(false, "unreachable");
 }
 
+// The output follows q's order of heads and tokens: when q's tokens are
+// outer to its heads (a head-split view of a [B, N, H * D] projection), out
+// is a head-transposed view of [B, Nq, H, Dv] memory, as PyTorch's
+// attention kernels return, so out.transpose(1, 2).reshape(B, Nq, H * Dv)
+// needs no copy; otherwise out is contiguous [B, H, Nq, Dv]. The fake
+// implementation (vectra_b200/custom_ops.py) applies the same rule.
+bool tokens_outer(const at::Tensor& q) {
+  return q.size(1) > 1 && q.size(2) > 1 && q.stride(2) > q.stride(1);
+}
+
+std::vector<int64_t> output_strides(const at::Tensor& q, int64_t dv) {
+  const int64_t h = q.size(1), n = q.size(2);
+  if (tokens_outer(q)) return {n * h * dv, dv, h * dv, 1};
+  return {h * n * dv, n * dv, dv, 1};
+}
+
+at::Tensor empty_output(const at::Tensor& q, const at::Tensor& v) {
+  const int64_t dv = v.size(3);
+  return at::empty_strided({q.size(0), q.size(1), q.size(2), dv},
+                           output_strides(q, dv), v.options());
+}
+
 // Validates, allocates the output and launches through the C ABI.
 at::Tensor run(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                const at::Tensor& scale,
@@ -91,21 +124,7 @@ at::Tensor run(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
   if (key_bias.has_value() && key_bias->defined())
     bias = side_input(*key_bias, q);
 
-  // The output follows q's order of heads and tokens: when q's tokens are
-  // outer to its heads (a head-split view of a [B, N, H * D] projection),
-  // out is a head-transposed view of [B, Nq, H, Dv] memory, as PyTorch's
-  // attention kernels return, so out.transpose(1, 2).reshape(B, Nq, H * Dv)
-  // needs no copy; otherwise out is contiguous [B, H, Nq, Dv]. The fake
-  // implementation (vectra_b200/custom_ops.py) applies the same rule.
-  const bool tokens_outer =
-      q.size(1) > 1 && q.size(2) > 1 && q.stride(2) > q.stride(1);
-  at::Tensor out =
-      tokens_outer
-          ? at::empty({q.size(0), q.size(2), q.size(1), v.size(3)},
-                      v.options())
-                .permute({0, 2, 1, 3})
-          : at::empty({q.size(0), q.size(1), q.size(2), v.size(3)},
-                      v.options());
+  at::Tensor out = empty_output(q, v);
   vectra_rbf_args a{};
   a.q = describe(q);
   a.k = describe(k);
@@ -137,6 +156,18 @@ at::Tensor rbf_attention_flags_cuda(const at::Tensor& q, const at::Tensor& k,
   return run(q, k, v, scale, key_bias, static_cast<uint32_t>(flags));
 }
 
+// The CPU implementation: same output layout rule as the CUDA one.
+at::Tensor rbf_attention_cpu_impl(const at::Tensor& q, const at::Tensor& k,
+                                  const at::Tensor& v, const at::Tensor& scale,
+                                  const std::optional<at::Tensor>& key_bias) {
+  TORCH_CHECK_VALUE(q.dim() == 4 && k.dim() == 4 && v.dim() == 4,
+                    "q, k and v must be rank 4 ([B, H, N, D])");
+  const int64_t dv = v.size(3);
+  return vectra_cpu::rbf_attention_cpu(
+      q, k, v, scale, key_bias, {q.size(0), q.size(1), q.size(2), dv},
+      output_strides(q, dv));
+}
+
 }  // namespace
 
 TORCH_LIBRARY(vectra, m) {
@@ -147,6 +178,10 @@ TORCH_LIBRARY(vectra, m) {
 
 TORCH_LIBRARY_IMPL(vectra, CUDA, m) {
   m.impl("rbf_attention", &rbf_attention_cuda);
+}
+
+TORCH_LIBRARY_IMPL(vectra, CPU, m) {
+  m.impl("rbf_attention", &rbf_attention_cpu_impl);
 }
 
 TORCH_LIBRARY(vectra_b200, m) {
