@@ -77,12 +77,11 @@ typedef struct {
   int64_t stride[4];
 } vectra_tensor;
 
-/* Kernel selection flags (0 = automatic). */
+/* Kernel selection flags (0 = automatic; bit 0x8 is retired and, like any
+ * other unknown bit, makes the call fail with VECTRA_ERR_FORCED). */
 #define VECTRA_FLAG_FORCE_GENERIC 0x1u /* the any-shape tiled kernel */
 #define VECTRA_FLAG_FORCE_DECODE  0x2u /* the Nq == 1 streaming kernel */
 #define VECTRA_FLAG_FORCE_TC      0x4u /* the tcgen05/TMEM tensor-core kernel */
-#define VECTRA_FLAG_FORCE_DECODE_MMA 0x8u /* the Nq == 1 tensor-core kernel
-                                              (never chosen automatically) */
 #define VECTRA_FLAG_FORCE_SMALL   0x10u /* the one-tile-per-plane kernel */
 
 /* Kernels (vectra_rbf_select_kernel's result). */
@@ -91,7 +90,7 @@ enum {
   VECTRA_KERNEL_GENERIC = 1,  /* rbf_generic: any shape, stride and dtype */
   VECTRA_KERNEL_DECODE = 2,   /* rbf_decode: Nq == 1, bulk-copy streaming */
   VECTRA_KERNEL_TC = 3,       /* rbf_tc: tcgen05 + TMEM, long sequences */
-  VECTRA_KERNEL_DECODE_MMA = 4, /* rbf_decode_mma: Nq == 1, mma.sync dots */
+  /* 4 is retired (an Nq == 1 mma.sync kernel, never chosen automatically) */
   VECTRA_KERNEL_SMALL = 5       /* rbf_small: Nk <= 128, mma.sync tiles */
 };
 
@@ -122,7 +121,7 @@ VECTRA_API int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* s
 VECTRA_API int vectra_rbf_select_kernel(const vectra_rbf_args* args);
 
 /* Name of a VECTRA_KERNEL_* value ("none", "generic", "decode", "tc",
- * "decode_mma", "small"). */
+ * "small"; "invalid" for any other value). */
 VECTRA_API const char* vectra_rbf_kernel_name(int kernel);
 
 /* Message for a status code. */

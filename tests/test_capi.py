@@ -43,7 +43,7 @@ def test_status_strings():
         'key_bias must be constant across queries')
     assert _lib.strerror(12345) == 'unknown status'
     assert [_lib.kernel_name(k) for k in range(6)] == [
-        'none', 'generic', 'decode', 'tc', 'decode_mma', 'small']
+        'none', 'generic', 'decode', 'tc', 'invalid', 'small']
 
 
 def test_build_info_names_the_architecture():
@@ -93,11 +93,10 @@ def test_serving_shape_selects_the_decode_kernel():
     assert _select(_args(bias_shape=(4, 1, 1, 64))) == _lib.KERNEL_DECODE
     assert _select(_args(d=128, dv=128)) == _lib.KERNEL_DECODE
     assert _select(_args(d=32, dv=32)) == _lib.KERNEL_DECODE
-    # The tensor-core decode kernel takes it only when pinned.
-    assert _select(_args(flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
-        _lib.KERNEL_DECODE_MMA)
-    assert _select(_args(d=128, dv=128, flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
-        _lib.KERNEL_DECODE_MMA)
+    # The retired flag bit (an mma.sync decode kernel), like any unknown
+    # bit, is refused rather than ignored.
+    assert _select(_args(flags=0x8)) == _lib.ERR_FORCED
+    assert _select(_args(flags=0x100)) == _lib.ERR_FORCED
 
 
 def test_config1_fp32_selects_decode():
@@ -147,11 +146,6 @@ def test_forced_kernels():
     assert _select(_args(flags=_lib.FLAG_FORCE_GENERIC)) == (
         _lib.KERNEL_GENERIC)
     assert _select(_args(nq=2, flags=_lib.FLAG_FORCE_DECODE)) == (
-        _lib.ERR_FORCED)
-    assert _select(_args(nq=2, flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
-        _lib.ERR_FORCED)
-    assert _select(_args(dtype=_lib.F32, d=64, dv=64,
-                         flags=_lib.FLAG_FORCE_DECODE_MMA)) == (
         _lib.ERR_FORCED)
 
 

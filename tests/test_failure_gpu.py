@@ -58,7 +58,6 @@ CASES = {
     'small': ((3, 2, 33, 65, 32), 'bf16', True),
     'tc': ((1, 2, 300, 200, 64), 'bf16', True),
     'generic': ((2, 3, 21, 37, 48), 'f32', True),
-    'decode_mma': ((5, 2, 1, 90, 128), 'f16', True),
 }
 
 
@@ -93,8 +92,8 @@ def test_output_guard_bands_are_untouched(kernel):
                'decode_masked': _lib.FLAG_FORCE_DECODE,
                'decode_masked_2chunks': _lib.FLAG_FORCE_DECODE,
                'small': _lib.FLAG_FORCE_SMALL,
-               'tc': _lib.FLAG_FORCE_TC, 'generic': _lib.FLAG_FORCE_GENERIC,
-               'decode_mma': _lib.FLAG_FORCE_DECODE_MMA}[kernel]
+               'tc': _lib.FLAG_FORCE_TC,
+               'generic': _lib.FLAG_FORCE_GENERIC}[kernel]
     assert _lib.LIB.vectra_rbf_select_kernel(ctypes.byref(a)) >= 0, kernel
     stream = torch.cuda.current_stream().cuda_stream
     assert _lib.LIB.vectra_rbf_attention_forward(

@@ -44,8 +44,6 @@ def _kernels_for(q_shape, d, dv, dtype, nk):
     if q_shape[2] == 1 and d == dv and (
             d in (32, 64, 128) if dtype != 'f32' else d in (32, 64)):
         kernels.append('decode')
-    if q_shape[2] == 1 and d == dv and d in (64, 128) and dtype != 'f32':
-        kernels.append('decode_mma')
     if (q_shape[2] >= 2 and nk <= 128 and d == dv and d in (32, 64)
             and dtype != 'f32'):
         kernels.append('small')

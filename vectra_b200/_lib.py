@@ -20,11 +20,9 @@ ERR_SCALE_SHAPE, ERR_BIAS_SHAPE, ERR_BIAS_QUERY = -5, -6, -7
 ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE, ERR_FORCED = -8, -9, -10, -11
 # kernel selection flags
 FLAG_FORCE_GENERIC, FLAG_FORCE_DECODE, FLAG_FORCE_TC = 0x1, 0x2, 0x4
-FLAG_FORCE_DECODE_MMA = 0x8
 FLAG_FORCE_SMALL = 0x10
 # kernels
 KERNEL_NONE, KERNEL_GENERIC, KERNEL_DECODE, KERNEL_TC = 0, 1, 2, 3
-KERNEL_DECODE_MMA = 4
 KERNEL_SMALL = 5
 
 # Every symbol include/vectra_rbf.h declares.
@@ -59,8 +57,8 @@ def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f'{LIB_PATH} is missing: build it with `python '
-            'vectra_b200/build.py` (nvcc, sm_100a). vectra_b200 has no CPU or '
-            'Triton fallback.')
+            'vectra_b200/build.py` (nvcc, sm_100a). CUDA tensors have no CPU '
+            'or Triton fallback.')
     lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
     lib.vectra_rbf_attention_forward.argtypes = [ctypes.POINTER(Args),
                                                  ctypes.c_void_p]

@@ -134,6 +134,11 @@ int build_problem(const vectra_rbf_args* a, RbfProblem* p) {
 }
 
 int select(const RbfProblem& p, uint32_t flags) {
+  constexpr uint32_t kKnownFlags = VECTRA_FLAG_FORCE_GENERIC |
+                                   VECTRA_FLAG_FORCE_DECODE |
+                                   VECTRA_FLAG_FORCE_TC |
+                                   VECTRA_FLAG_FORCE_SMALL;
+  if (flags & ~kKnownFlags) return VECTRA_ERR_FORCED;
   if (p.B == 0 || p.H == 0 || p.Nq == 0 || p.Dv == 0)
     return VECTRA_KERNEL_NONE;
   if (flags & VECTRA_FLAG_FORCE_GENERIC) return VECTRA_KERNEL_GENERIC;
@@ -141,14 +146,10 @@ int select(const RbfProblem& p, uint32_t flags) {
     return decode_supports(p) ? VECTRA_KERNEL_DECODE : VECTRA_ERR_FORCED;
   if (flags & VECTRA_FLAG_FORCE_TC)
     return tc_supports(p) ? VECTRA_KERNEL_TC : VECTRA_ERR_FORCED;
-  if (flags & VECTRA_FLAG_FORCE_DECODE_MMA)
-    return decode_mma_supports(p) ? VECTRA_KERNEL_DECODE_MMA
-                                  : VECTRA_ERR_FORCED;
   if (flags & VECTRA_FLAG_FORCE_SMALL)
     return small_supports(p) ? VECTRA_KERNEL_SMALL : VECTRA_ERR_FORCED;
-  // Nq == 1: the SIMT decode kernel measured faster than the mma.sync one on
-  // every serving shape tried (config 2: 26.3 us against 28.7 us; config 3:
-  // 170 us against 178 us), so the tensor-core decode kernel is opt-in.
+  // Nq == 1: the SIMT decode kernel (an mma.sync variant measured slower
+  // on every serving shape tried and is not built).
   if (decode_supports(p)) return VECTRA_KERNEL_DECODE;
   if (tc_supports(p)) return VECTRA_KERNEL_TC;
   if (small_supports(p)) return VECTRA_KERNEL_SMALL;
@@ -220,9 +221,6 @@ int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* stream) {
     case VECTRA_KERNEL_TC:
       err = launch_tc(p, s);
       break;
-    case VECTRA_KERNEL_DECODE_MMA:
-      err = launch_decode_mma(p, s);
-      break;
     case VECTRA_KERNEL_SMALL:
       err = launch_small(p, s);
       break;
@@ -245,8 +243,6 @@ const char* vectra_rbf_kernel_name(int kernel) {
       return "decode";
     case VECTRA_KERNEL_TC:
       return "tc";
-    case VECTRA_KERNEL_DECODE_MMA:
-      return "decode_mma";
     case VECTRA_KERNEL_SMALL:
       return "small";
     default:

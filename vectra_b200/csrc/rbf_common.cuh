@@ -340,8 +340,6 @@ cudaError_t launch_generic(const RbfProblem& p, cudaStream_t stream);
 cudaError_t launch_decode(const RbfProblem& p, cudaStream_t stream);
 // True when the decode kernel has an instantiation and the layout it needs.
 bool decode_supports(const RbfProblem& p);
-cudaError_t launch_decode_mma(const RbfProblem& p, cudaStream_t stream);
-bool decode_mma_supports(const RbfProblem& p);
 cudaError_t launch_tc(const RbfProblem& p, cudaStream_t stream);
 bool tc_supports(const RbfProblem& p);
 cudaError_t launch_small(const RbfProblem& p, cudaStream_t stream);

@@ -9,10 +9,12 @@ through libvectra_rbf.so. Differences from the reference, on purpose:
 * There is no Triton path and no "CUDA without Triton -> CPU arithmetic"
   fallback (custom_ops.py:39-42,83-84): if the extension is missing,
   importing this module raises.
-* There is no CPU implementation: the operator runs on CUDA tensors only and
-  raises NotImplementedError for CPU tensors. The reference's CPU
-  arithmetic (reference.matmul_rbf_attention) is the oracle here, not
-  product code.
+* CPU tensors run this library's CPU implementation (csrc/rbf_cpu.cpp, a
+  C++ loop parallel over planes), the counterpart of the reference's
+  default implementation (custom_ops.py:52-72 ->
+  reference.matmul_rbf_attention): float32 arithmetic, result in v's
+  dtype, key_bias broadcast to [B, H, Nq, Nk]. Dispatch is by device, as
+  in the reference; CUDA tensors never reach it.
 * The output's layout follows q (`output_strides`): when q's tokens are
   outer to its heads (q a head-split view of a [B, N, H * D] projection,
   as in the compiled model), the output is a head-transposed view of
@@ -75,8 +77,8 @@ def rbf_attention(q, k, v, scale, key_bias=None) -> torch.Tensor:
     """Fused RBF attention: softmax(-scale * ||q - k||^2 + key_bias) @ v.
 
     Args:
-      q: [B, H, Nq, D] CUDA tensor (float32, float16 or bfloat16), any
-        strides.
+      q: [B, H, Nq, D] (float32, float16 or bfloat16), any strides; CUDA
+        tensors run the sm_100a kernels, CPU tensors the CPU implementation.
       k: [B, H, Nk, D], same dtype.
       v: [B, H, Nk, Dv], same dtype.
       scale: Broadcastable to [B, H, 1, 1]; the RBF coefficient
@@ -97,15 +99,14 @@ def rbf_attention(q, k, v, scale, key_bias=None) -> torch.Tensor:
 
 KERNELS = {'generic': _lib.FLAG_FORCE_GENERIC,
            'decode': _lib.FLAG_FORCE_DECODE,
-           'decode_mma': _lib.FLAG_FORCE_DECODE_MMA,
            'tc': _lib.FLAG_FORCE_TC,
            'small': _lib.FLAG_FORCE_SMALL}
 
 
 def rbf_attention_with_kernel(q, k, v, scale, key_bias=None,
                               kernel: str = 'auto') -> torch.Tensor:
-    """The same operator with the kernel pinned ('generic', 'decode',
-    'decode_mma', 'tc', 'small').
+    """The same operator with the kernel pinned ('generic', 'decode', 'tc',
+    'small').
 
     Raises ValueError when the pinned kernel cannot run the problem.
     """
@@ -131,7 +132,7 @@ def _describe(t):
 
 def kernel_for(q, k, v, scale, key_bias=None, kernel: str = 'auto') -> str:
     """Name of the kernel the operator launches for these tensors
-    ('decode', 'decode_mma', 'tc', 'small', 'generic' or 'none'); raises
+    ('decode', 'tc', 'small', 'generic' or 'none'); raises
     ValueError when the arguments are invalid. Launches nothing."""
     import ctypes  # pylint: disable=import-outside-toplevel
     a = _lib.Args()
