@@ -34,43 +34,30 @@ def pytest_collection_modifyitems(config, items):
         item.add_marker(skip)
 
 
-REF = os.path.join(ROOT, 'baseline', '_ref')
-
-
 def compile_pass_installed():
-    """Whether the reference's compile pass (installed unmodified into
-    baseline/_ref) is here."""
-    return os.path.isdir(os.path.join(REF, 'vectra_compiler'))
+    """Whether the build installed the reference's compile pass and price
+    model (unmodified) into baseline/_ref. When it did, the tests that use
+    them run, and fail if they cannot load them."""
+    from tests import reference_swap  # pylint: disable=import-outside-toplevel
+    return reference_swap.installed()
+
+
+@pytest.fixture(scope='session')
+def reference():
+    """The reference's compile pass (`backend`), price model (`model`) and
+    export module (`compile_entry`) from baseline/_ref, with the module name
+    its replacement imports to register the operator
+    (compiler/vectra_compiler/replacement.py:38-39) bound to this library
+    (the one-file swap of kernels/vectra_kernels/custom_ops.py,
+    tests/reference_swap/custom_ops.py)."""
+    if not compile_pass_installed():
+        pytest.skip('the reference is not installed in baseline/_ref (no '
+                    'reference checkout at build time)')
+    from tests import reference_swap  # pylint: disable=import-outside-toplevel
+    return reference_swap.load_reference()
 
 
 @pytest.fixture(scope='module')
-def backend():
-    """The reference's `vectra_compiler.backend`, with the module name its
-    replacement imports to register the operator
-    (compiler/vectra_compiler/replacement.py:38-39) bound to
-    `vectra_b200.custom_ops` (the one-file swap of
-    kernels/vectra_kernels/custom_ops.py)."""
-    if not compile_pass_installed():
-        pytest.skip('the reference compile pass is not installed in '
-                    'baseline/_ref')
-    import types  # pylint: disable=import-outside-toplevel
-    import vectra_b200  # pylint: disable=import-outside-toplevel,unused-import
-    from vectra_b200 import custom_ops  # pylint: disable=import-outside-toplevel
-    names = ('vectra_kernels', 'vectra_kernels.custom_ops')
-    saved = {n: sys.modules.get(n) for n in names}
-    pkg = types.ModuleType('vectra_kernels')
-    pkg.__path__ = []
-    pkg.custom_ops = custom_ops
-    sys.modules['vectra_kernels'] = pkg
-    sys.modules['vectra_kernels.custom_ops'] = custom_ops
-    sys.path.insert(0, REF)
-    try:
-        from vectra_compiler import backend as b  # pylint: disable=import-outside-toplevel
-        yield b
-    finally:
-        sys.path.remove(REF)
-        for n, m in saved.items():
-            if m is None:
-                sys.modules.pop(n, None)
-            else:
-                sys.modules[n] = m
+def backend(reference):  # pylint: disable=redefined-outer-name
+    """The reference's `vectra_compiler.backend` (see `reference`)."""
+    return reference.backend
