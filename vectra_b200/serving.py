@@ -23,6 +23,15 @@ A model compiled with this library's operator (the compile pass rewrites
 every RBF-attention site to torch.ops.vectra.rbf_attention) replays its
 kernels inside the graph; the operator makes no host synchronisation and no
 allocation the capture cannot serve.
+
+A compiled forward that reads a device value on the host cannot be
+captured. The reference's price model is one: its radius trim is a
+torch.cond (models/price_transformer/model.py:96-138), and Inductor
+evaluates the predicate with `.item()` in the generated wrapper before it
+picks a branch. `capture=False` serves such a model with everything above
+except the graph: the same static slots, device-side padding, pinned
+staging and copy/compute overlap, with the compiled forward called on the
+slot's static inputs for every chunk.
 """
 
 from __future__ import annotations
@@ -91,12 +100,17 @@ class GraphServingModel:
       slots: Static batches in flight (2: one being copied in while the
         other runs).
       warmup: Eager calls on a side stream before the captures.
+      capture: Capture each slot's forward in a CUDA graph (True), or call
+        the compiled forward on the slot's inputs for every chunk (False:
+        for forwards that synchronise with the host, which a capture
+        forbids).
 
     `predict` is not thread-safe: one instance serves one caller stream.
     """
 
     def __init__(self, compiled: Callable, example_inputs: Sequence[
-            torch.Tensor], slots: int = 2, warmup: int = 2):
+            torch.Tensor], slots: int = 2, warmup: int = 2,
+                 capture: bool = True):
         example = list(example_inputs)
         if not example:
             raise ValueError('example_inputs is empty')
@@ -111,6 +125,7 @@ class GraphServingModel:
         if slots < 1:
             raise ValueError(f'slots must be >= 1, got {slots}')
         self.compiled = compiled
+        self.captured = bool(capture)
         self.batch_size = b
         self.device = device
         self._shapes = [(t.dtype, tuple(t.shape[1:])) for t in example]
@@ -126,11 +141,15 @@ class GraphServingModel:
             for _ in range(warmup):
                 self.compiled(*self._slots[0].inputs)
         torch.cuda.current_stream().wait_stream(side)
-        pool = torch.cuda.graph_pool_handle()
+        pool = torch.cuda.graph_pool_handle() if self.captured else None
         for slot in self._slots:
-            slot.graph = torch.cuda.CUDAGraph()
-            with torch.no_grad(), torch.cuda.graph(slot.graph, pool=pool):
-                slot.output = self.compiled(*slot.inputs)
+            if self.captured:
+                slot.graph = torch.cuda.CUDAGraph()
+                with torch.no_grad(), torch.cuda.graph(slot.graph, pool=pool):
+                    slot.output = self.compiled(*slot.inputs)
+            else:
+                with torch.no_grad():
+                    slot.output = self.compiled(*slot.inputs)
             if not isinstance(slot.output, torch.Tensor):
                 raise TypeError('the compiled model must return one tensor')
             if slot.output.dim() < 1 or slot.output.shape[0] != \
@@ -182,7 +201,11 @@ class GraphServingModel:
                 compute.wait_event(slot.copied)
                 for t in slot.inputs:
                     pad_in_place(t, size)
-                slot.graph.replay()
+                if self.captured:
+                    slot.graph.replay()
+                else:
+                    with torch.no_grad():
+                        slot.output = self.compiled(*slot.inputs)
                 out[start:stop].copy_(slot.output[:size])
                 slot.released.record(compute)
                 slot.released_valid = True

@@ -23,6 +23,17 @@ configuration descriptions instead, with fixed seeds:
    projection values ~ N(0,1)/sqrt(D); the coefficient 1/(2 sigma_h^2) with
    log sigma_h ~ N(0.7, 0.3); a [B,1,1,N] bf16 key bias of zeros (every
    comparable valid).
+
+`price_model_inputs` builds the whole price model's inputs for benchmark
+config 5 (the reference's `PricingInputs`, models/price_transformer/
+model.py:58-88, in forward-argument order): targets and comparables placed
+uniformly over a 50 km box, comparables' log sale prices ~ N(13, 0.6^2)
+(lognormal prices), standardised attributes ~ N(0, 1), embeddings
+tanh(N(0, 1)) as the reference's `example_inputs` draws them
+(model.py:252-282), sale days up to a few years before the valuation day,
+GeoHash-6 cells of the locations, every comparable valid, and a 50 km
+search radius, so every request has comparables inside its radius and the
+model's radius trim takes its cheap branch.
 """
 
 import dataclasses
@@ -172,3 +183,88 @@ def algorithmic_flops(w: Workload) -> int:
     B, H, nq, D = w.q.shape
     nk, dv = w.k.shape[2], w.v.shape[3]
     return 2 * B * H * nq * nk * (D + dv)
+
+
+# Benchmark config 5: the price model's serving shape.
+PRICE_MODEL = dict(embedding_dim=128, attribute_dim=48, d_model=256,
+                   num_heads=8, num_layers=4, ffn_dim=1024, num_candidates=64)
+PRICE_BATCH = 1024
+PRICE_RADIUS_KM = 50.0
+_BOX_CENTRE = (37.7749, -122.4194)  # degrees (latitude, longitude)
+_BOX_KM = 50.0
+_KM_PER_DEGREE = 6371.0088 * math.pi / 180.0
+
+
+def geohash_cells(lat: torch.Tensor, lng: torch.Tensor,
+                  precision: int = 6) -> torch.Tensor:
+    """GeoHash cells as integers (int64): 5 * precision bits, longitude and
+    latitude bisection bits interleaved, longitude first, most significant
+    bit first (the GeoHash definition; data/geo.py:107 in the reference).
+    A coordinate's index on an axis with n bits is floor((x - lo) /
+    (hi - lo) * 2^n), the result of n bisections."""
+    lng_bits = (5 * precision + 1) // 2
+    lat_bits = 5 * precision // 2
+
+    def index(x, lo, hi, bits):
+        scaled = ((x.double() - lo) / (hi - lo) * (1 << bits)).floor()
+        return scaled.clamp(0, (1 << bits) - 1).long()
+
+    col = index(lng, -180.0, 180.0, lng_bits)
+    row = index(lat, -90.0, 90.0, lat_bits)
+    cell = torch.zeros_like(col)
+    for i in range(5 * precision):
+        if i % 2 == 0:
+            lng_bits -= 1
+            bit = (col >> lng_bits) & 1
+        else:
+            lat_bits -= 1
+            bit = (row >> lat_bits) & 1
+        cell = (cell << 1) | bit
+    return cell
+
+
+def price_model_inputs(batch: int = PRICE_BATCH, seed: int = 0,
+                       device='cpu', config=None):
+    """Benchmark config 5's inputs for the price model: 13 tensors in the
+    forward's argument order (query_embedding, query_attributes,
+    query_location, query_cell6, valuation_day, radius_km, cand_embedding,
+    cand_attributes, cand_log_price, cand_sale_day, cand_location,
+    cand_cell6, cand_valid). Generated on the CPU from `seed`, then moved to
+    `device`."""
+    cfg = dict(PRICE_MODEL if config is None else config)
+    e, a, k = cfg['embedding_dim'], cfg['attribute_dim'], \
+        cfg['num_candidates']
+    gen = torch.Generator().manual_seed(seed)
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=gen)
+
+    def rand(*shape):
+        return torch.rand(*shape, generator=gen)
+
+    half_lat = 0.5 * _BOX_KM / _KM_PER_DEGREE
+    half_lng = half_lat / math.cos(math.radians(_BOX_CENTRE[0]))
+
+    def locations(*shape):
+        lat = _BOX_CENTRE[0] + half_lat * (2 * rand(*shape) - 1)
+        lng = _BOX_CENTRE[1] + half_lng * (2 * rand(*shape) - 1)
+        return torch.stack([lat, lng], dim=-1)
+
+    query_location = locations(batch)
+    cand_location = locations(batch, k)
+    tensors = (
+        torch.tanh(randn(batch, e)),
+        randn(batch, a),
+        query_location,
+        geohash_cells(query_location[..., 0], query_location[..., 1]),
+        torch.full((batch,), 20000.0),
+        torch.full((batch,), PRICE_RADIUS_KM),
+        torch.tanh(randn(batch, k, e)),
+        randn(batch, k, a),
+        13.0 + 0.6 * randn(batch, k),
+        20000.0 - 900.0 * randn(batch, k).abs(),
+        cand_location,
+        geohash_cells(cand_location[..., 0], cand_location[..., 1]),
+        torch.ones(batch, k, dtype=torch.bool),
+    )
+    return tuple(t.to(device) for t in tensors)
