@@ -1,20 +1,23 @@
 """Benchmark of torch.ops.vectra.rbf_attention on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C]
-                    [--impl vectra|reference]
+                    [--impl vectra|reference] [--scaling strong|weak]
 
 One step is one pass of the operator over one batch of the workload
 (default: benchmark config 2, the serving shape B=1024, H=8, Lq=1, Lk=64,
-D=64, bf16). With N GPUs (torchrun, one process per GPU) every rank
-processes its own batch of the same size (weak scaling; queries are
-independent, there is no collective on the data path) and the value is the
-total queries of all ranks divided by the slowest rank's device time.
-`--scaling strong` splits one batch of the configured size across the
-ranks instead (contiguous shards of identically seeded data).
+D=64, bf16). With N GPUs (torchrun, one process per GPU) the batch is
+sharded (strong scaling, the default): every rank generates the same seeded
+batch and keeps its contiguous slice (vectra_b200.sharding.shard_range), so
+the ranks together do the one-GPU job; there is no collective on the data
+path. The value is the batch's queries divided by the slowest rank's device
+time. `--scaling weak` gives every rank its own batch of the configured
+size instead; with N > 1 the strong line also carries the weak figure
+(`extra.weak`).
 
 Rank 0 prints one JSON line with:
 * value: queries/s (or TFLOP/s for config 4), inputs resident in HBM,
-  CUDA events over exactly K steps bracketed by barrier + synchronize;
+  CUDA events over exactly K steps bracketed by barrier + synchronize,
+  max over ranks;
 * e2e: the same metric through the public API with pinned host buffers,
   host->device input copies and the device->host output copy of every step
   inside the timed region (steps pipelined over a copy and a compute
@@ -25,6 +28,8 @@ Rank 0 prints one JSON line with:
   implementation (reference.matmul_rbf_attention, the default impl of
   vectra::rbf_attention) timed on this host's cores on a bounded sample
   (rank 0, N == 1 only);
+* extra.long_sequence (config 2, N == 1): benchmark config 4 (B=16, H=16,
+  L=4096, D=128) through the tensor-core kernel, TFLOP/s by CUDA events;
 * clocks: nvidia-smi samples taken while the GPU ran the kernel.
 
 `--impl reference` times the reference's CPU implementation of the path
@@ -32,11 +37,14 @@ Rank 0 prints one JSON line with:
 reference.matmul_rbf_attention, reference.py:79-99, through the oracle's
 NumPy port: the reference is Python and ships no compiled CPU code; the
 port is also ~2.6x faster here than the port of the eager chain) with all
-host threads on bounded samples of the same workload.
+host threads on bounded samples of the same workload. It never loads this
+library: the seeded generators are read from vectra_b200/workloads.py by
+path, and its `config` is the GPU line's, key for key.
 """
 
 import argparse
 import concurrent.futures
+import importlib.util
 import json
 import os
 import re
@@ -63,20 +71,23 @@ def parse_args(argv=None):
     p.add_argument('--impl', default='vectra', choices=('vectra',
                                                          'reference'))
     p.add_argument('--e2e-steps', type=int, default=20)
-    p.add_argument('--scaling', default='weak', choices=('weak', 'strong'),
-                   help='weak: each GPU runs the configured batch; strong: '
-                        'the GPUs split one configured batch')
+    p.add_argument('--scaling', default='strong', choices=('strong', 'weak'),
+                   help='strong: the GPUs split one configured batch; weak: '
+                        'each GPU runs the configured batch')
     p.add_argument('--graph-calls', type=int, default=0,
                    help='operator calls per replayed CUDA graph in the timed '
                         'region (0: a multiple of the input sets, >= 12)')
     p.add_argument('--cpu-seconds', type=float, default=10.0)
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-extra', action='store_true',
+                   help='skip the extra measurements (weak scaling at N > 1, '
+                        'config 4 at N == 1)')
     p.add_argument('--profile', action='store_true',
                    help='warm-up and K steps only (for ncu): no clock soak, '
                         'no e2e, no CPU baseline, no JSON line')
     p.add_argument('--model', action='store_true',
-                   help='config 5 only: the whole compiled model served from '
-                        'CUDA graphs (predictions/s) instead of one site')
+                   help='config 5 only: the reference price model compiled '
+                        'whole (predictions/s) instead of one site')
     p.add_argument('--scan', choices=('l2', 'pq'),
                    help='the index-shard scan path instead of the operator: '
                         'exhaustive L2 or PQ top-k (queries/s)')
@@ -92,11 +103,26 @@ def parse_args(argv=None):
 # Shared descriptions
 # ---------------------------------------------------------------------------
 
+def workloads_module():
+    """vectra_b200/workloads.py, loaded from its file (torch only): the
+    reference arm and the CPU baseline use the seeded generators without
+    importing the package, whose import loads this library's kernels."""
+    name = 'vectra_bench_workloads'
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(
+            name, os.path.join(ROOT, 'vectra_b200', 'workloads.py'))
+        module = importlib.util.module_from_spec(spec)
+        sys.modules[name] = module
+        spec.loader.exec_module(module)
+    return sys.modules[name]
+
+
 def metric_for(config, model=False):
     if model:
-        return ('price-model predictions/s, compiled forward with 3 RBF '
-                'sites rewritten (B=1024 targets x 65 tokens, d_model 256, '
-                'H=8 D=32, bf16), CUDA-graph serving', 'predictions/s')
+        return ('price-model predictions/s, compiled PriceTransformer with '
+                'every RBF site rewritten (B=1024 targets x 65 tokens, '
+                'd_model 256, 4 layers, H=8 D=32, bf16 blocks)',
+                'predictions/s')
     if config == 5:
         return ('RBF-attn compiled-model site targets/s (B=1024 N=65 H=8 '
                 'D=32 bf16, strided q/k/v)', 'targets/s')
@@ -105,6 +131,40 @@ def metric_for(config, model=False):
                 'bf16)', 'TFLOP/s')
     return ('RBF-attn queries/s @B=1024 + achieved HBM GB/s vs 8 TB/s, '
             '1/2/4/8 B200', 'queries/s')
+
+
+def plan(config, scaling, world):
+    """Batch sizes and input rotation of a run, from the shapes alone (both
+    arms report them): the largest per-GPU batch, the job's batch, one
+    input set's bytes on a GPU, and how many sets rotate so the timed calls
+    read more than L2 holds."""
+    w = workloads_module()
+    b, h, nq, nk, d, dt = w.SHAPES[config]
+    es = 4 if dt == 'f32' else 2
+    strong = scaling == 'strong'
+    per_gpu = -(-b // world) if strong else b
+    bias = nk * 2 if config in (3, 5) else 0  # a bf16 bias row per batch row
+    set_bytes = per_gpu * (h * (nq + nk) * 2 * d * es + bias) + h * 4
+    n_sets = max(1, min(32 if strong else 8, -(-3 * L2_BYTES // set_bytes)))
+    return {'per_gpu': per_gpu, 'global_batch': b if strong else b * world,
+            'set_bytes': set_bytes, 'n_sets': n_sets}
+
+
+def line_config(args, world):
+    """The JSON line's `config`, the same in both arms."""
+    w = workloads_module()
+    p = plan(args.config, args.scaling, world)
+    total = p['n_sets'] * p['set_bytes']
+    return {
+        'workload': w.NAMES[args.config],
+        'queries_per_gpu': p['per_gpu'],
+        'global_batch': p['global_batch'],
+        'parallelism': f'batch-sharded x{world} ({args.scaling} scaling), '
+                       'no collective',
+        'l2': f'{p["n_sets"]} rotating input sets of '
+              f'{p["set_bytes"] / 1e6:.1f} MB per GPU '
+              f'({total / 2**20:.0f} MiB in all; L2 {L2_BYTES >> 20} MiB)',
+    }
 
 
 def peaks():
@@ -142,9 +202,8 @@ def ncu_traffic(config, name=None, key='dram_bytes_per_launch_full'):
 
 def cpu_sample(config, n_queries, seed=1):
     """A bounded host-side sample of the workload (same generator rules)."""
-    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
-    w = workloads.make(config, device='cpu', seed=seed,
-                       batch=n_queries if config != 4 else 1)
+    w = workloads_module().make(config, device='cpu', seed=seed,
+                                batch=n_queries if config != 4 else 1)
     tensors = [None if t is None else t.float().numpy() for t in w.tensors()]
     return w, tensors
 
@@ -224,10 +283,9 @@ def time_cpu(config, seconds, threads, formulation='matmul'):
 
 def run_reference(args):
     rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
     if rank != 0:
         return 0
-    sys.path.insert(0, ROOT)
-    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
     metric, unit = metric_for(args.config)
     threads = os.cpu_count() or 1
     # About two minutes in all, whatever K and W are (at least 20 ms of
@@ -245,13 +303,14 @@ def run_reference(args):
     line = {
         'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
         'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
-        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
-        'dtype': 'f32', 'data': 'synthetic (seeded, benchmark config shapes)',
-        'config': {'workload': workloads.NAMES[args.config],
-                   'device': 'host CPU', 'threads': cores},
+        'higher_is_better': True, 'scaling': args.scaling,
+        'vs_baseline': None, 'dtype': 'f32',
+        'data': 'synthetic (seeded; benchmark config shapes and '
+                'distributions)',
+        'config': line_config(args, world),
         'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
                          'kind': 'port', 'sample': sample,
-                         'cpu_model': cpu_model()},
+                         'cpu_model': cpu_model(), 'device': 'host CPU'},
         'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     }
@@ -313,106 +372,53 @@ class ClockSampler:
                 'samples': len(sm)}
 
 
-def run_vectra(args):
-    import torch  # pylint: disable=import-outside-toplevel
-    import torch.distributed as dist  # pylint: disable=import-outside-toplevel
-    sys.path.insert(0, ROOT)
-    import vectra_b200  # pylint: disable=import-outside-toplevel
-    from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
-    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+class Gpu:
+    """The rank's device, process group and timing helpers."""
 
-    world = int(os.environ.get('WORLD_SIZE', '1'))
-    rank = int(os.environ.get('RANK', '0'))
-    local = int(os.environ.get('LOCAL_RANK', '0'))
-    torch.cuda.set_device(local)
-    dev = torch.device('cuda', local)
-    distributed = world > 1
-    if distributed:
+    def __init__(self, timeout_s=300):
         import datetime  # pylint: disable=import-outside-toplevel
-        dist.init_process_group('nccl', device_id=dev,
-                                timeout=datetime.timedelta(seconds=300))
+        import torch  # pylint: disable=import-outside-toplevel
+        import torch.distributed as dist  # pylint: disable=import-outside-toplevel
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get('WORLD_SIZE', '1'))
+        self.rank = int(os.environ.get('RANK', '0'))
+        self.local = int(os.environ.get('LOCAL_RANK', '0'))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device('cuda', self.local)
+        self.distributed = self.world > 1
+        if self.distributed:
+            dist.init_process_group(
+                'nccl', device_id=self.dev,
+                timeout=datetime.timedelta(seconds=timeout_s))
 
-    def barrier():
-        if distributed:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
+    def barrier(self):
+        if self.distributed:
+            self.dist.barrier(device_ids=[self.local])
+        self.torch.cuda.synchronize()
 
-    def max_over_ranks(x):
-        return sharding.max_over_ranks(x, device=dev)
+    def max_over_ranks(self, x):
+        from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
+        return sharding.max_over_ranks(x, device=self.dev)
 
-    # Weak scaling (default): every rank has its own batch of the configured
-    # size. Strong scaling: every rank generates the same global batch and
-    # keeps its contiguous shard (sharding.shard_range), so the ranks
-    # together do the 1-GPU job.
-    strong = args.scaling == 'strong'
+    def close(self):
+        if self.distributed:
+            self.dist.destroy_process_group()
 
-    def make_set(i):
-        if not strong:
-            return workloads.make(args.config, device=dev,
-                                  seed=1000 * rank + i)
-        full = workloads.make(args.config, device=dev, seed=i)
-        lo, hi = sharding.shard_range(full.batch, world, rank)
-        part = full.slice(lo, hi)
-        return workloads.Workload(
-            part.config, part.dtype,
-            *(None if t is None else t.clone()
-              for t in (part.q, part.k, part.v, part.scale, part.key_bias,
-                        part.lengths)))
 
-    w0 = make_set(0)
-    global_batch = (workloads.SHAPES[args.config][0] if strong
-                    else w0.batch * world)
-    set_bytes = max(1, workloads.dense_bytes(w0))
-    n_sets = max(1, min(32 if strong else 8, -(-3 * L2_BYTES // set_bytes)))
-    sets = [w0] + [make_set(i) for i in range(1, n_sets)]
-    alg_bytes = workloads.algorithmic_bytes(w0)
-    flops = workloads.algorithmic_flops(w0)
-    queries = w0.batch
-    op = torch.ops.vectra.rbf_attention
-    stream = torch.cuda.current_stream(dev)
-
-    def step(i):
-        w = sets[i % n_sets]
-        return op(w.q, w.k, w.v, w.scale, w.key_bias)
-
-    # Warm-up (also loads the module and sets kernel attributes), then a
-    # short soak so the clock sampler sees the GPU under this load (the
-    # sampler keeps running through the timed region).
-    for i in range(max(3, args.warmup)):
-        step(i)
-    if args.profile:
-        # One NVTX range per operator call, named as the reference's
-        # benchmarks name theirs (kernels/benchmarks/bandwidth.py:74-77),
-        # so ncu --nvtx --nvtx-include vectra_region/ selects the same work.
-        for i in range(args.steps):
-            torch.cuda.nvtx.range_push('vectra_region')
-            step(i)
-            torch.cuda.nvtx.range_pop()
-        torch.cuda.synchronize()
-        if distributed:
-            dist.destroy_process_group()
-        return 0
-    sampler = ClockSampler(local)
-    torch.cuda.synchronize()
-    t_soak = time.perf_counter()
-    i = 0
-    while time.perf_counter() - t_soak < 0.6:
-        step(i)
-        i += 1
-        if i % 64 == 0:
-            torch.cuda.synchronize()
-
-    # Timed region: exactly K steps, one operator call on one batch each,
-    # call t on input set t mod n_sets. The calls are replayed from CUDA
-    # graphs that hold G consecutive calls (G = the smallest multiple of
-    # n_sets that is at least 12), so the host's per-call dispatch never
-    # starves the GPU and consecutive kernels are not separated by graph
-    # launches; a second graph holds the K mod G calls left over. Timed with
-    # CUDA events on the launching stream.
-    per_graph = args.graph_calls or n_sets * -(-12 // n_sets)
-    per_graph = max(1, min(per_graph, args.steps))
-    full, rest = divmod(args.steps, per_graph)
-    capture_stream = torch.cuda.Stream(dev)
+def graph_timed(gpu, step, n_sets, steps, graph_calls=0):
+    """Times exactly `steps` calls of step(i) (call i on input set i mod
+    n_sets) replayed from CUDA graphs that hold G consecutive calls (G = the
+    smallest multiple of n_sets that is at least 12, or `graph_calls`), so
+    the host's per-call dispatch never starves the GPU; a second graph holds
+    the calls left over. Returns (device ms of the region, this library's
+    launches in it, G)."""
+    import vectra_b200  # pylint: disable=import-outside-toplevel
+    torch = gpu.torch
+    stream = torch.cuda.current_stream(gpu.dev)
+    per_graph = graph_calls or n_sets * -(-12 // n_sets)
+    per_graph = max(1, min(per_graph, steps))
+    full, rest = divmod(steps, per_graph)
+    capture_stream = torch.cuda.Stream(gpu.dev)
     capture_stream.wait_stream(stream)
 
     def capture(n_calls):
@@ -435,7 +441,7 @@ def run_vectra(args):
         rest_graph.replay()
     region0 = torch.cuda.Event(enable_timing=True)
     region1 = torch.cuda.Event(enable_timing=True)
-    barrier()
+    gpu.barrier()
     region0.record(stream)
     for _ in range(full):
         main_graph.replay()
@@ -443,17 +449,123 @@ def run_vectra(args):
         rest_graph.replay()
     region1.record(stream)
     torch.cuda.synchronize()
-    barrier()
+    gpu.barrier()
     launches = full * main_launches + rest_launches
     region_ms = region0.elapsed_time(region1)
+    del main_graph, rest_graph
+    return region_ms, launches, per_graph
+
+
+def long_sequence_extra(gpu, calls=20):
+    """Benchmark config 4 through the operator (the tensor-core kernel),
+    CUDA events over `calls` back-to-back calls on two input sets of 1 GB
+    each (> L2): TFLOP/s and the fraction of the measured bf16 peak."""
+    import vectra_b200  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+    torch = gpu.torch
+    sets = [workloads.make(4, device=gpu.dev, seed=s) for s in range(2)]
+    op = torch.ops.vectra.rbf_attention
+    for i in range(3):
+        op(*sets[i % 2].tensors())
+    stream = torch.cuda.current_stream(gpu.dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    before = vectra_b200.launch_count()
+    e0.record(stream)
+    for i in range(calls):
+        op(*sets[i % 2].tensors())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / calls
+    flops = workloads.algorithmic_flops(sets[0])
+    _, tflops_peak, kind = peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    out = {'workload': workloads.NAMES[4],
+           'kernel': vectra_b200.kernel_for(*sets[0].tensors()),
+           'ms_per_call': ms, 'value': tflops, 'unit': 'TFLOP/s',
+           'calls': calls, 'launches': vectra_b200.launch_count() - before,
+           'frac_of_bf16_peak': tflops / tflops_peak,
+           'peak': tflops_peak, 'peak_kind': f'bf16 dense, {kind} (burst)'}
+    del sets
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_vectra(args):
+    sys.path.insert(0, ROOT)
+    gpu = Gpu()
+    torch = gpu.torch
+    import vectra_b200  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
+    from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
+    world, rank, dev = gpu.world, gpu.rank, gpu.dev
+
+    def make_set(i, scaling):
+        """Input set i on this rank: its shard of the identically seeded
+        batch (strong) or its own batch (weak)."""
+        if scaling == 'weak':
+            return workloads.make(args.config, device=dev,
+                                  seed=1000 * rank + i)
+        full = workloads.make(args.config, device=dev, seed=i)
+        lo, hi = sharding.shard_range(full.batch, world, rank)
+        part = full.slice(lo, hi)
+        return workloads.Workload(
+            part.config, part.dtype,
+            *(None if t is None else t.clone()
+              for t in (part.q, part.k, part.v, part.scale, part.key_bias,
+                        part.lengths)))
+
+    p = plan(args.config, args.scaling, world)
+    n_sets = p['n_sets']
+    sets = [make_set(i, args.scaling) for i in range(n_sets)]
+    w0 = sets[0]
+    alg_bytes = workloads.algorithmic_bytes(w0)
+    flops = workloads.algorithmic_flops(w0)
+    op = torch.ops.vectra.rbf_attention
+
+    def step(i):
+        w = sets[i % n_sets]
+        return op(w.q, w.k, w.v, w.scale, w.key_bias)
+
+    # Warm-up (also loads the module and sets kernel attributes), then a
+    # short soak so the clock sampler sees the GPU under this load (the
+    # sampler keeps running through the timed region).
+    for i in range(max(3, args.warmup)):
+        step(i)
+    if args.profile:
+        # One NVTX range per operator call, named as the reference's
+        # benchmarks name theirs (kernels/benchmarks/bandwidth.py:74-77),
+        # so ncu --nvtx --nvtx-include vectra_region/ selects the same work.
+        for i in range(args.steps):
+            torch.cuda.nvtx.range_push('vectra_region')
+            step(i)
+            torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        gpu.close()
+        return 0
+    sampler = ClockSampler(gpu.local)
+    torch.cuda.synchronize()
+    t_soak = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_soak < 0.6:
+        step(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+
+    # Timed region: exactly K steps, one operator call on one batch (shard)
+    # each, replayed from CUDA graphs, timed with CUDA events on the
+    # launching stream, max over ranks.
+    region_ms, launches, per_graph = graph_timed(gpu, step, n_sets,
+                                                 args.steps, args.graph_calls)
     # Back-to-back kernels keep the GPU busy, so the kernel's average launch
     # duration is the region over K (an upper bound: it includes the small
     # gaps between kernels).
     kernel_ms = region_ms / args.steps
     clocks = sampler.stop()
-    slowest_ms = max_over_ranks(region_ms)
+    slowest_ms = gpu.max_over_ranks(region_ms)
     ms_per_step = slowest_ms / args.steps
-    del main_graph, rest_graph
 
     # End to end through the public API: every step copies its inputs in
     # from pinned host memory, runs the operator and copies its result out.
@@ -501,18 +613,41 @@ def run_vectra(args):
         e2e_step(i)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    barrier()
+    gpu.barrier()
     e0.record(copy_stream)
     for i in range(e2e_steps):
         e2e_step(i)
     e1.record(compute_stream)
     torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    gpu.barrier()
+    e2e_ms = gpu.max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+
+    # Extras, outside the timed regions: the weak-scaling figure (N > 1,
+    # every rank its own full batch) and benchmark config 4 (N == 1).
+    extra = {}
+    if not args.no_extra and world > 1:
+        other = 'weak' if args.scaling == 'strong' else 'strong'
+        alt = plan(args.config, other, world)
+        del sets
+        sets = [make_set(i, other) for i in range(alt['n_sets'])]
+        n_sets = alt['n_sets']
+        for i in range(3):
+            step(i)
+        steps_alt = min(args.steps, 500)
+        alt_ms, _, _ = graph_timed(gpu, step, n_sets, steps_alt)
+        alt_step = gpu.max_over_ranks(alt_ms) / steps_alt
+        extra[other] = {'value': alt['global_batch'] / (alt_step * 1e-3),
+                        'unit': metric_for(args.config)[1],
+                        'ms_per_step': alt_step, 'steps': steps_alt,
+                        'queries_per_gpu': alt['per_gpu'],
+                        'global_batch': alt['global_batch']}
+    if not args.no_extra and world == 1 and args.config == 2:
+        extra['long_sequence'] = long_sequence_extra(gpu)
 
     # Rank 0 reports.
     metric, unit = metric_for(args.config)
     hbm, tflops_peak, peak_kind = peaks()
+    global_batch = p['global_batch']
     if args.config == 4:
         job_flops = flops * global_batch / w0.batch
         value = job_flops / (ms_per_step * 1e-3) / 1e12
@@ -528,7 +663,9 @@ def run_vectra(args):
         achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
         roof = {'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
                 'unit': 'GB/s', 'frac': achieved / hbm,
-                'traffic': ncu_traffic(args.config),
+                'traffic': (ncu_traffic(args.config) * w0.batch /
+                            workloads.SHAPES[args.config][0]
+                            if ncu_traffic(args.config) else None),
                 'peak_kind': f'HBM copy, {peak_kind}',
                 'algorithmic_bytes_per_launch': alg_bytes,
                 'vs_8tbs': achieved / 8000.0}
@@ -551,30 +688,26 @@ def run_vectra(args):
             'dtype': w0.dtype,
             'data': 'synthetic (seeded; benchmark config shapes and '
                     'distributions)',
-            'config': {
-                'workload': workloads.NAMES[args.config],
-                'queries_per_gpu': queries, 'global_batch': global_batch,
-                'parallelism': f'batch-sharded x{world} ({args.scaling} '
-                               'scaling), no collective',
-                'graph_calls': per_graph,
-                'l2': f'{n_sets} rotating input sets of '
-                      f'{set_bytes / 1e6:.0f} MB (> L2 {L2_BYTES >> 20} MiB)',
-                'kernel': vectra_b200.kernel_for(*w0.tensors()),
-            },
+            'config': line_config(args, world),
+            'launch': {'kernel': vectra_b200.kernel_for(*w0.tensors()),
+                       'graph_calls': per_graph,
+                       'queries_this_rank': w0.batch},
             'e2e': {'value': e2e_value, 'unit': unit,
-                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                    'h2d_bytes_per_step': h2d * world,
+                    'd2h_bytes_per_step': d2h * world,
+                    'h2d_bytes_per_step_per_gpu': h2d,
                     'steps': e2e_steps, 'pipelined': True,
                     # what bounds it: the host->device copy of the inputs
-                    'h2d_gbs': h2d / (e2e_ms * 1e-3) / 1e9},
+                    'h2d_gbs_per_gpu': h2d / (e2e_ms * 1e-3) / 1e9},
             'gpu_launches': launches,
             'kernel_ms_per_launch': kernel_ms,
             'roofline': roof,
             'cpu_baseline': cpu,
+            'extra': extra,
             'clocks': clocks,
         }
         emit(line)
-    if distributed:
-        dist.destroy_process_group()
+    gpu.close()
     return 0
 
 
@@ -582,43 +715,58 @@ def run_vectra(args):
 # Config 5 at the model level (--model)
 # ---------------------------------------------------------------------------
 
-MODEL_BATCH = 1024      # targets per served batch (benchmark config 5)
-MODEL_LAYERS = 3        # RBF-attention sites
 MODEL_E2E_CHUNKS = 8    # served batches per end-to-end request
+MODEL_SETS = 4          # rotating resident input batches
 
 
-def load_compile_pass():
-    """The reference's compile pass, installed unmodified in baseline/_ref,
-    with the module name its replacement imports to register the operator
-    (compiler/vectra_compiler/replacement.py:38-39) bound to this library's
-    custom_ops (the one-file swap of kernels/vectra_kernels/custom_ops.py).
-    """
-    import types  # pylint: disable=import-outside-toplevel
-    from vectra_b200 import custom_ops  # pylint: disable=import-outside-toplevel
+def load_reference_model_only():
+    """The reference's price model (models.price_transformer.model) from its
+    unmodified install in baseline/_ref, without the compile pass and
+    without this library: the eager model the reference arm times."""
     ref = os.path.join(ROOT, 'baseline', '_ref')
-    if not os.path.isdir(os.path.join(ref, 'vectra_compiler')):
-        raise SystemExit('--model needs the reference compile pass in '
-                         'baseline/_ref')
-    pkg = types.ModuleType('vectra_kernels')
-    pkg.__path__ = []
-    pkg.custom_ops = custom_ops
-    sys.modules['vectra_kernels'] = pkg
-    sys.modules['vectra_kernels.custom_ops'] = custom_ops
-    sys.path.insert(0, ref)
-    from vectra_compiler import backend  # pylint: disable=import-outside-toplevel
-    return backend
+    if not os.path.isfile(os.path.join(ref, 'INSTALL.json')):
+        return None
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from models.price_transformer import model  # pylint: disable=import-outside-toplevel
+    return model
 
 
-def time_cpu_model(seconds, threads, batch=64):
-    """The model's eager forward on the host CPU (float32, the eager RBF
-    chain at every site, `threads` intra-op threads) over a fixed sample
-    of `batch` targets: (predictions/s, cores, sample)."""
+def model_batch(args, world):
+    w = workloads_module()
+    if args.scaling == 'strong':
+        return -(-w.PRICE_BATCH // world), w.PRICE_BATCH
+    return w.PRICE_BATCH, w.PRICE_BATCH * world
+
+
+def model_config_line(args, world):
+    """The model line's `config`, the same in both arms."""
+    w = workloads_module()
+    per_gpu, global_batch = model_batch(args, world)
+    return {
+        'workload': 'config 5 model: the reference PriceTransformer '
+                    '(embedding 128, 48 attributes, d_model 256, 4 layers, '
+                    '8 heads of 32, ffn 1024, 64 comparables), random init, '
+                    f'radius {w.PRICE_RADIUS_KM:g} km',
+        'queries_per_gpu': per_gpu, 'global_batch': global_batch,
+        'parallelism': f'batch-sharded x{world} ({args.scaling} scaling), '
+                       'no collective',
+        'l2': 'activations of a batch exceed L2 (17 MB per 65 x 256 bf16 '
+              'tensor per 1,024 targets; ~40 live per forward)',
+    }
+
+
+def time_cpu_model(model_lib, seconds, threads, batch=64):
+    """The reference's eager price model on the host CPU (float32, the eager
+    RBF chain at every site, `threads` intra-op threads) over a fixed
+    sample of `batch` targets: (predictions/s, cores, sample)."""
     import torch  # pylint: disable=import-outside-toplevel
-    from tests import spatial_model  # pylint: disable=import-outside-toplevel
+    w = workloads_module()
     torch.set_num_threads(threads)
     torch.manual_seed(0)
-    model = spatial_model.SpatialNet(layers=MODEL_LAYERS).eval()
-    args = spatial_model.inputs(batch, seed=1)
+    model = model_lib.PriceTransformer(
+        model_lib.ModelConfig(**w.PRICE_MODEL)).eval()
+    args = w.price_model_inputs(batch, seed=1)
     with torch.no_grad():
         model(*args)  # warm-up
         t0 = time.perf_counter()
@@ -627,35 +775,44 @@ def time_cpu_model(seconds, threads, batch=64):
             model(*args)
             n += 1
         value = n * batch / (time.perf_counter() - t0)
-    return value, threads, (f'eager float32 model forward, {batch} targets '
-                            f'x 65 tokens per pass, {threads} threads')
+    return value, threads, (f'eager float32 reference model forward, '
+                            f'{batch} targets x 65 tokens per pass, '
+                            f'{threads} threads')
 
 
 def run_model_reference(args):
-    """The reference arm at the model level: the eager model on the host's
-    cores (the reference's CPU path for config 5: every site runs the
-    eager RBF chain)."""
+    """The reference arm at the model level: the reference's eager price
+    model on the host's cores (its CPU path for config 5: every site runs
+    the eager RBF chain)."""
     if int(os.environ.get('RANK', '0')) != 0:
         return 0
-    sys.path.insert(0, ROOT)
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    model_lib = load_reference_model_only()
+    if model_lib is None:
+        emit({'impl': 'reference',
+              'unavailable': 'the reference price model is not installed in '
+                             'baseline/_ref (no reference checkout at build '
+                             'time)'})
+        return 0
     metric, unit = metric_for(5, model=True)
     threads = os.cpu_count() or 1
     per_step = max(0.05, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
-        time_cpu_model(per_step / 4, threads)
-    runs = [time_cpu_model(per_step, threads) for _ in range(args.steps)]
+        time_cpu_model(model_lib, per_step / 4, threads)
+    runs = [time_cpu_model(model_lib, per_step, threads)
+            for _ in range(args.steps)]
     value = float(statistics.median(r[0] for r in runs))
     _, cores, sample = runs[0]
     emit({
         'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit,
         'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
-        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
-        'dtype': 'f32', 'data': 'synthetic (seeded, random-init weights)',
-        'config': {'workload': 'config 5 model', 'device': 'host CPU',
-                   'threads': cores},
+        'higher_is_better': True, 'scaling': args.scaling,
+        'vs_baseline': None, 'dtype': 'f32',
+        'data': 'synthetic (seeded inputs, random-init weights)',
+        'config': model_config_line(args, world),
         'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores,
-                         'kind': 'port', 'sample': sample,
-                         'cpu_model': cpu_model()},
+                         'kind': 'reference', 'sample': sample,
+                         'cpu_model': cpu_model(), 'device': 'host CPU'},
         'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     })
@@ -663,115 +820,121 @@ def run_model_reference(args):
 
 
 def run_model(args):
-    """Config 5 served whole: the compiled model (every RBF site rewritten
-    to this library's operator by the reference's compile pass) captured
-    in CUDA graphs and served through vectra_b200.serving.
+    """Config 5 served whole: the reference's PriceTransformer (4 layers,
+    bf16 blocks), compiled by the reference's compile_entry with every RBF
+    site rewritten to this library's operator (the one-file swap), after the
+    reference's numerics gate.
 
-    value: predictions/s with the requests resident in HBM, one step = one
-    served batch of 1,024 targets (GraphServingModel.predict: copy into a
-    static batch, replay, float result). e2e: one step = one request of
-    8 x 1,024 targets from pinned host memory through predict, result
-    copied back to the host. The forward's activations (34 MB per tensor
-    per layer) exceed L2, so no flush is needed between steps.
+    value: predictions/s with the batches resident in HBM, one step = one
+    compiled forward of a served batch (1,024 targets, or the rank's shard
+    of them). The forward cannot be captured in a CUDA graph: its radius
+    trim is a torch.cond whose predicate Inductor reads on the host. e2e:
+    one step = one request of 8 batches from pinned host memory through
+    vectra_b200.serving (static slots, pinned staging, copy/compute
+    overlap), result read back to the host.
     """
-    import torch  # pylint: disable=import-outside-toplevel
-    import torch.distributed as dist  # pylint: disable=import-outside-toplevel
     sys.path.insert(0, ROOT)
+    gpu = Gpu(timeout_s=900)
+    torch = gpu.torch
     import vectra_b200  # pylint: disable=import-outside-toplevel
+    from tests import reference_swap  # pylint: disable=import-outside-toplevel
     from vectra_b200 import serving  # pylint: disable=import-outside-toplevel
-    from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
     from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
-    from tests import spatial_model  # pylint: disable=import-outside-toplevel
+    world, rank, dev = gpu.world, gpu.rank, gpu.dev
 
-    world = int(os.environ.get('WORLD_SIZE', '1'))
-    rank = int(os.environ.get('RANK', '0'))
-    local = int(os.environ.get('LOCAL_RANK', '0'))
-    torch.cuda.set_device(local)
-    dev = torch.device('cuda', local)
-    distributed = world > 1
-    if distributed:
-        import datetime  # pylint: disable=import-outside-toplevel
-        dist.init_process_group('nccl', device_id=dev,
-                                timeout=datetime.timedelta(seconds=600))
-
-    def barrier():
-        if distributed:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
-
-    backend = load_compile_pass()
+    ref = reference_swap.load_reference()
+    per_gpu, global_batch = model_batch(args, world)
+    cfg = ref.model.ModelConfig(**workloads.PRICE_MODEL)
+    spec = ref.compile_entry.ServingSpec(device=str(dev), batch_size=per_gpu,
+                                         block_dtype='bfloat16')
     torch.manual_seed(0)
-    model = spatial_model.SpatialNet(layers=MODEL_LAYERS).to(dev).eval()
-    model = model.to(torch.bfloat16)
-    example = spatial_model.inputs(MODEL_BATCH, device=dev,
-                                   dtype=torch.bfloat16, seed=1000 * rank)
-    compiled, report = backend.compile_for_serving(
-        model, example, expected_sites=MODEL_LAYERS)
-    if report.sites != MODEL_LAYERS or report.graph_break_count:
-        raise SystemExit(f'compile pass rewrote {report.sites} sites with '
+    eager = ref.compile_entry.prepare(ref.model.PriceTransformer(cfg), spec)
+    compiled, report, compile_s = ref.compile_entry.compile_model(eager, spec)
+    if report.sites != cfg.num_layers or report.graph_break_count:
+        raise SystemExit(f'compile pass rewrote {report.sites} of '
+                         f'{cfg.num_layers} sites with '
                          f'{report.graph_break_count} graph breaks')
-    before = vectra_b200.launch_count()
-    gs = serving.GraphServingModel(compiled, example)
-    per_capture = (vectra_b200.launch_count() - before) // (2 + 2)
-    sets = [spatial_model.inputs(MODEL_BATCH, device=dev,
-                                 dtype=torch.bfloat16, seed=1000 * rank + i)
-            for i in range(1, 5)]
+    # The reference's serving check before traffic (load_bundle): compiled
+    # vs eager on a seeded batch at rtol 1e-3 / atol 1e-3.
+    gate, _ = ref.compile_entry.max_abs_error(compiled, eager, cfg, spec,
+                                              batches=1)
+
+    def shard(seed):
+        full = workloads.price_model_inputs(global_batch if args.scaling ==
+                                            'strong' else per_gpu, seed=seed)
+        if args.scaling == 'strong':
+            lo = min(rank * per_gpu, global_batch - per_gpu)
+            full = tuple(t[lo:lo + per_gpu] for t in full)
+        return full
+
+    sets = [tuple(t.to(dev) for t in shard(1000 * (args.scaling == 'weak')
+                                           * rank + i))
+            for i in range(MODEL_SETS)]
+    distance = ref.model.microhood.haversine_km(sets[0][2], sets[0][10])
+    cheap_branch = bool((sets[0][12] & (distance <= sets[0][5][:, None]))
+                        .any(-1).all())
     stream = torch.cuda.current_stream(dev)
+
+    def forward(i):
+        with torch.no_grad():
+            return compiled(*sets[i % MODEL_SETS])
+
     for i in range(max(3, args.warmup)):
-        gs.predict(sets[i % len(sets)])
-    sampler = ClockSampler(local)
+        forward(i)
+    sampler = ClockSampler(gpu.local)
     torch.cuda.synchronize()
     t_soak = time.perf_counter()
     i = 0
     while time.perf_counter() - t_soak < 0.6:
-        gs.predict(sets[i % len(sets)])
+        forward(i)
         i += 1
-        if i % 8 == 0:
-            torch.cuda.synchronize()
 
-    # Timed region: exactly K served batches.
+    # Timed region: exactly K compiled forwards.
     r0 = torch.cuda.Event(enable_timing=True)
     r1 = torch.cuda.Event(enable_timing=True)
-    barrier()
+    gpu.barrier()
+    before = vectra_b200.launch_count()
     r0.record(stream)
     for i in range(args.steps):
-        gs.predict(sets[i % len(sets)])
+        forward(i)
     r1.record(stream)
     torch.cuda.synchronize()
-    barrier()
+    launches = vectra_b200.launch_count() - before
+    gpu.barrier()
     clocks = sampler.stop()
     region_ms = r0.elapsed_time(r1)
-    ms_per_step = sharding.max_over_ranks(region_ms, device=dev) / args.steps
-    value = MODEL_BATCH * world / (ms_per_step * 1e-3)
+    ms_per_step = gpu.max_over_ranks(region_ms) / args.steps
+    value = global_batch / (ms_per_step * 1e-3)
 
     # End to end: requests of 8 served batches from pinned host memory,
-    # result read back to the host; the chunks of one request pipeline
-    # their host-to-device copies under the previous chunk's forward.
-    n_e2e = MODEL_E2E_CHUNKS * MODEL_BATCH
-    host = [t.pin_memory() for t in spatial_model.inputs(
-        n_e2e, dtype=torch.bfloat16, seed=7 + rank)]
+    # result read back to the host.
+    served = serving.GraphServingModel(compiled, sets[0], capture=False)
+    n_e2e = MODEL_E2E_CHUNKS * per_gpu
+    host = [t.pin_memory() for t in workloads.price_model_inputs(
+        n_e2e, seed=7 + rank)]
     h2d = sum(t.numel() * t.element_size() for t in host)
     e2e_steps = max(3, min(args.e2e_steps, args.steps))
     for _ in range(2):
-        gs.predict(host).cpu()
+        served.predict(host).cpu()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    barrier()
+    gpu.barrier()
     e0.record(stream)
     for _ in range(e2e_steps):
-        result = gs.predict(host).cpu()
+        result = served.predict(host).cpu()
     e1.record(stream)
     torch.cuda.synchronize()
-    barrier()
+    gpu.barrier()
     d2h = result.numel() * result.element_size()
-    e2e_ms = sharding.max_over_ranks(e0.elapsed_time(e1),
-                                     device=dev) / e2e_steps
-    e2e_value = n_e2e * world / (e2e_ms * 1e-3)
+    e2e_ms = gpu.max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    e2e_value = MODEL_E2E_CHUNKS * global_batch / (e2e_ms * 1e-3)
 
     # The site kernel on its own, on the sites' shapes (benchmark config 5's
-    # site workload), event-timed over back-to-back calls.
+    # site workload at the rank's batch), event-timed over back-to-back
+    # calls.
     hbm, _, peak_kind = peaks()
-    site_sets = [workloads.make(5, device=dev, seed=i) for i in range(4)]
+    site_sets = [workloads.make(5, device=dev, seed=i, batch=per_gpu)
+                 for i in range(4)]
     op = torch.ops.vectra.rbf_attention
     for w in site_sets:
         op(*w.tensors())
@@ -789,36 +952,36 @@ def run_model(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = time_cpu_model(args.cpu_seconds,
+        v, cores, sample = time_cpu_model(ref.model, args.cpu_seconds,
                                           os.cpu_count() or 1)
         cpu = {'value': v, 'unit': 'predictions/s', 'cores': cores,
-               'kind': 'port', 'sample': sample, 'cpu_model': cpu_model()}
+               'kind': 'reference', 'sample': sample,
+               'cpu_model': cpu_model()}
     if rank == 0:
         metric, unit = metric_for(5, model=True)
         emit({
             'metric': metric, 'value': value, 'unit': unit, 'n_gpus': world,
             'steps': args.steps, 'warmup': args.warmup,
             'ms_per_step': ms_per_step, 'higher_is_better': True,
-            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
+            'scaling': args.scaling, 'vs_baseline': None, 'dtype': 'bf16',
             'data': 'synthetic (seeded inputs, random-init weights)',
-            'config': {
-                'workload': 'config 5 model: compiled 3-block price-model-'
-                            'style network (tests/spatial_model.py), '
-                            f'{MODEL_BATCH} targets x 65 tokens per batch',
-                'global_batch': MODEL_BATCH * world,
-                'parallelism': f'one served batch per GPU x{world}, no '
-                               'collective',
-                'compile': {'sites': report.sites,
-                            'graph_count': report.graph_count,
-                            'graph_break_count': report.graph_break_count},
-                'serving': 'vectra_b200.serving.GraphServingModel, 2 slots',
-                'l2': 'activations 34 MB per tensor per layer (> L2)',
-            },
+            'config': model_config_line(args, world),
+            'compile': {'sites': report.sites, 'matches': report.matches,
+                        'graph_count': report.graph_count,
+                        'graph_break_count': report.graph_break_count,
+                        'seconds': compile_s,
+                        'numerics_gate_max_abs_error': gate,
+                        'radius_branch': ('within_radius (cheap)'
+                                          if cheap_branch else
+                                          'with_fallback')},
             'e2e': {'value': e2e_value, 'unit': unit,
-                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                    'h2d_bytes_per_step': h2d * world,
+                    'd2h_bytes_per_step': d2h * world,
                     'steps': e2e_steps,
-                    'targets_per_step': n_e2e},
-            'gpu_launches': per_capture * args.steps,
+                    'targets_per_step': MODEL_E2E_CHUNKS * global_batch,
+                    'serving': 'vectra_b200.serving.GraphServingModel, '
+                               '2 slots, capture=False'},
+            'gpu_launches': launches,
             'roofline': {
                 'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
                 'unit': 'GB/s', 'frac': achieved / hbm,
@@ -827,14 +990,13 @@ def run_model(args):
                 'kernel': 'rbf_small, one site, timed alone',
                 'algorithmic_bytes_per_launch': alg_bytes,
                 'site_ms': site_ms,
-                'sites_share_of_forward': MODEL_LAYERS * site_ms /
+                'sites_share_of_forward': cfg.num_layers * site_ms /
                                           ms_per_step},
             'cpu_baseline': cpu,
             'clocks': clocks,
         })
-    del gs
-    if distributed:
-        dist.destroy_process_group()
+    del served
+    gpu.close()
     return 0
 
 

@@ -4,18 +4,33 @@ summaries in profiles/ (the GPU arm runs on a B200 only)."""
 
 import json
 import os
+import subprocess
+import sys
 
 import pytest
 
 import bench
+from tests import reference_swap
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_defaults_are_the_headline_config_on_one_gpu():
     a = bench.parse_args([])
-    assert (a.gpus, a.config, a.impl, a.scaling) == (1, 2, 'vectra', 'weak')
+    assert (a.gpus, a.config, a.impl, a.scaling) == (1, 2, 'vectra',
+                                                     'strong')
     assert a.warmup >= 3
+
+
+@pytest.mark.parametrize('world', [1, 2, 8])
+def test_strong_scaling_splits_one_batch(world):
+    p = bench.plan(2, 'strong', world)
+    assert p['global_batch'] == 1024 and p['per_gpu'] == 1024 // world
+    w = bench.plan(2, 'weak', world)
+    assert w['global_batch'] == 1024 * world and w['per_gpu'] == 1024
+    # The rotating input sets read more than L2 holds (or 32 sets).
+    assert (p['n_sets'] * p['set_bytes'] > 3 * bench.L2_BYTES or
+            p['n_sets'] == 32)
 
 
 def test_reference_arm_prints_one_json_line(capfd, monkeypatch):
@@ -34,6 +49,33 @@ def test_reference_arm_prints_one_json_line(capfd, monkeypatch):
     assert cpu['kind'] == 'port' and cpu['cpu_model']
     assert line['e2e'] == {'value': line['value'], 'unit': unit,
                            'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}
+    # The same config as the GPU arm's line, key for key.
+    assert line['config'] == bench.line_config(bench.parse_args(
+        ['--config', '1']), 1)
+
+
+def test_reference_arm_never_loads_this_library(tmp_path):
+    # In a fresh process: the arm's line is printed, no vectra_b200 module
+    # is imported and none of this library's shared objects is mapped.
+    probe = tmp_path / 'probe.py'
+    probe.write_text(
+        'import sys\n'
+        f'sys.path.insert(0, {ROOT!r})\n'
+        'import bench\n'
+        "bench.main(['--impl', 'reference', '--config', '2', '--steps', '1',"
+        " '--warmup', '0'])\n"
+        "mods = [m for m in sys.modules if m.startswith('vectra_b200')]\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print('MODS', mods)\n"
+        "print('MAPPED', 'libvectra_rbf' in maps or "
+        "'_vectra_rbf_torch' in maps)\n")
+    env = dict(os.environ)
+    env.pop('RANK', None)
+    out = subprocess.run([sys.executable, str(probe)], capture_output=True,
+                         text=True, check=True, env=env, timeout=600).stdout
+    lines = out.strip().splitlines()
+    assert json.loads(lines[0])['impl'] == 'reference'
+    assert 'MODS []' in out and 'MAPPED False' in out, out
 
 
 @pytest.mark.parametrize('config', [1, 2, 3, 4, 5])
@@ -60,6 +102,8 @@ def test_model_mode_needs_config_5():
     assert bench.metric_for(5, model=True)[1] == 'predictions/s'
 
 
+@pytest.mark.skipif(not reference_swap.installed(),
+                    reason='the reference is not installed in baseline/_ref')
 def test_model_reference_arm_prints_one_json_line(capfd, monkeypatch):
     monkeypatch.delenv('RANK', raising=False)
     assert bench.main(['--impl', 'reference', '--config', '5', '--model',
@@ -69,7 +113,10 @@ def test_model_reference_arm_prints_one_json_line(capfd, monkeypatch):
     line = json.loads(out[0])
     assert line['impl'] == 'reference' and line['unit'] == 'predictions/s'
     assert line['value'] > 0 and line['cpu_baseline']['cores'] >= 1
+    assert line['cpu_baseline']['kind'] == 'reference'
     assert line['e2e']['h2d_bytes_per_step'] == 0
+    assert line['config'] == bench.model_config_line(
+        bench.parse_args(['--config', '5', '--model']), 1)
 
 
 @pytest.mark.parametrize('kind', ['l2', 'pq'])
