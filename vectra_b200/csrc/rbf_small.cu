@@ -19,9 +19,15 @@
 //    kStages ahead.
 //  * Logits are 2 g q.k_j - g ||k_j||^2 + b_j in the exp2 domain (the
 //    row-constant -g ||q||^2 cancels in the softmax). The key terms
-//    (b_j - g ||k_j||^2) log2(e) are formed once per item by the CTA's
-//    threads from the staged K; the scale and bias loads are issued before
-//    the stage wait so their latency overlaps it.
+//    (b_j - g ||k_j||^2) log2(e) are formed once per item from the staged
+//    K by every thread of the CTA (two adjacent lanes per key when the CTA
+//    has two threads per key, each taking half of the key's chunks, joined
+//    by one shuffle), so no warp waits long at the barrier that publishes
+//    them; the scale and bias loads are issued before the stage wait so
+//    their latency overlaps it.
+//  * Item coordinates (b, h, query block) advance by a fixed step per item
+//    (no integer division in the loop); the row sums use packed f32x2
+//    adds.
 //  * S = Q K^T and O = P V on mma.sync m16n8k16 (bf16/f16 in, f32
 //    accumulate): Q fragments by ldmatrix, K fragments by ldmatrix, V
 //    fragments by ldmatrix.trans. All of a plane's keys are in the tile, so
@@ -46,6 +52,10 @@ namespace {
 #define VECTRA_SMALL_STAGES 2
 #endif
 constexpr int kStages = VECTRA_SMALL_STAGES;
+// 1: two threads per key form the key terms when the CTA has 2 NKP threads.
+#ifndef VECTRA_SMALL_SPLIT_KEYS
+#define VECTRA_SMALL_SPLIT_KEYS 1
+#endif
 
 struct SmallLaunch {
   int qr;           // queries per item (16 W)
@@ -79,7 +89,65 @@ __device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t addr,
   return old;
 }
 
-template <typename T, int D, int NKP>
+// Packed float32 pairs (sm_100a f32x2 arithmetic): logits and the
+// softmax's subtract and sum take one instruction per two elements.
+__device__ __forceinline__ uint64_t f2pk(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ float2 f2upk(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (b, h, query block) of a CTA's items, walked without divisions: item i of
+// the CTA is global item blockIdx.x + i * gridDim.x, and consecutive items
+// differ by gridDim.x = (db planes of H, dh heads, dq query blocks).
+struct ItemCursor {
+  int b, h, qb;
+  __device__ void init(int item, const SmallLaunch& L) {
+    const int plane = item / L.nqb;
+    qb = item - plane * L.nqb;
+    b = plane / L.H;
+    h = plane - b * L.H;
+  }
+  __device__ void advance(int dq, int dh, int db, const SmallLaunch& L) {
+    qb += dq;
+    int carry = 0;
+    if (qb >= L.nqb) {
+      qb -= L.nqb;
+      carry = 1;
+    }
+    h += dh + carry;
+    if (h >= L.H) {
+      h -= L.H;
+      b += 1;
+    }
+    b += db;
+  }
+};
+
+// PARTS threads (adjacent lanes) share a key's norm: each takes CH / PARTS
+// of its 16-byte chunks and they add their partial sums with a shuffle, so
+// the key terms are spread over every thread of the CTA.
+template <typename T, int D, int NKP, int PARTS>
 __global__ void __launch_bounds__(256)
     rbf_small_kernel(const __grid_constant__ CUtensorMap tq,
                      const __grid_constant__ CUtensorMap tk,
@@ -92,7 +160,9 @@ __global__ void __launch_bounds__(256)
   constexpr int NT = NKP / 8;      // 8-key n-tiles of S
   constexpr int KS = D / 16;       // 16-dim k-steps of S
   constexpr int DT = D / 8;        // 8-dim n-tiles of O
-  constexpr int BPT = 4;           // bias values a thread prefetches (max)
+  // Key-term slots per thread: with two threads per key the CTA has at
+  // least 2 NKP threads, so one slot covers the tile.
+  constexpr int BPT = PARTS == 2 ? 1 : 4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -107,7 +177,8 @@ __global__ void __launch_bounds__(256)
   const int nk = static_cast<int>(p.Nk);
   const int nq = static_cast<int>(p.Nq);
   const uint32_t tx_bytes = uint32_t(L.qr * RB + 2 * NKP * RB);
-
+  static_assert(PARTS == 1 || PARTS == 2, "key-term split");
+  static_assert(CH % PARTS == 0, "chunks per part");
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_addr(&full[s]), 1);
@@ -124,42 +195,49 @@ __global__ void __launch_bounds__(256)
       L.n_items > int(blockIdx.x)
           ? (L.n_items - 1 - int(blockIdx.x)) / int(gridDim.x) + 1
           : 0;
-  auto coords = [&](int i, int& b, int& h, int& qb) {
-    const int item = int(blockIdx.x) + i * int(gridDim.x);
-    const int plane = item / L.nqb;
-    qb = item - plane * L.nqb;
-    b = plane / L.H;
-    h = plane - b * L.H;
-  };
-  auto issue = [&](int i) {  // one thread
-    int b, h, qb;
-    coords(i, b, h, qb);
+  const int gstep = int(gridDim.x);
+  const int dq = gstep % L.nqb, dplanes = gstep / L.nqb;
+  const int dh = dplanes % L.H, db = dplanes / L.H;
+  auto issue = [&](int i, const ItemCursor& cur) {  // one thread
     const int s = i % kStages;
     uint8_t* st = stages + size_t(s) * L.stage_bytes;
     const uint32_t bar = smem_addr(&full[s]);
     mbar_arrive_expect_tx(bar, tx_bytes);
-    tma_load_4d(smem_addr(st), &tq, bar, 0, qb * L.qr, h, b);
-    tma_load_4d(smem_addr(st + L.k_off), &tk, bar, 0, 0, h, b);
-    tma_load_4d(smem_addr(st + L.v_off), &tv, bar, 0, 0, h, b);
+    tma_load_4d(smem_addr(st), &tq, bar, 0, cur.qb * L.qr, cur.h, cur.b);
+    tma_load_4d(smem_addr(st + L.k_off), &tk, bar, 0, 0, cur.h, cur.b);
+    tma_load_4d(smem_addr(st + L.v_off), &tv, bar, 0, 0, cur.h, cur.b);
   };
+  // Every thread walks `cur` (item i) without divisions; the thread that
+  // refills a stage places its item (i + kStages) from scratch.
+  ItemCursor cur;
+  cur.init(int(blockIdx.x), L);
   if (tid == 0)
-    for (int i = 0; i < kStages && i < my_items; ++i) issue(i);
+    for (int i = 0; i < kStages && i < my_items; ++i) {
+      ItemCursor at;
+      at.init(int(blockIdx.x) + i * gstep, L);
+      issue(i, at);
+    }
 
   for (int i = 0; i < my_items; ++i) {
-    int b, h, qb;
-    coords(i, b, h, qb);
+    const int b = cur.b, h = cur.h, qb = cur.qb;
+    cur.advance(dq, dh, db, L);
     const int s = i % kStages;
     uint8_t* st = stages + size_t(s) * L.stage_bytes;
     float* term = terms + s * NKP;
 
-    // Scale and this thread's key biases, loaded before the stage wait.
+    // Scale and the key biases this thread finalises (its keys u / PARTS,
+    // u = tid + t * nthreads, where u % PARTS == 0), loaded before the stage
+    // wait so their latency overlaps it. (Loading them a whole item ahead
+    // measured slower: the registers they hold cost more than they hide.)
     const float gamma = load_scale(p, b, h);
     float bias[BPT];
 #pragma unroll
     for (int t = 0; t < BPT; ++t) {
-      const int j = tid + t * nthreads;
+      const int u = tid + t * nthreads;
+      const int j = u / PARTS;
       bias[t] = 0.f;
-      if (j < nk && p.bias != nullptr) bias[t] = load_bias(p, b, h, j);
+      if (u % PARTS == 0 && j < nk && p.bias != nullptr)
+        bias[t] = load_bias(p, b, h, j);
     }
 
     const bool ok = mbar_wait_sleep(smem_addr(&full[s]),
@@ -168,15 +246,15 @@ __global__ void __launch_bounds__(256)
       // Key terms (b_j - g ||k_j||^2) log2(e); -inf for padded keys.
 #pragma unroll
       for (int t = 0; t < BPT; ++t) {
-        const int j = tid + t * nthreads;
-        if (j >= NKP) break;
-        float v = kNegInf;
+        const int u = tid + t * nthreads;
+        if (u - lane >= NKP * PARTS) break;  // warp-uniform
+        const int j = u / PARTS, part = u % PARTS;
+        float acc = 0.f;
         if (j < nk) {
-          float acc = 0.f;
 #pragma unroll
-          for (int ch = 0; ch < CH; ++ch) {
+          for (int cc = 0; cc < CH / PARTS; ++cc) {
             const uint4 raw = *reinterpret_cast<const uint4*>(
-                st + L.k_off + swz<RB>(j, ch));
+                st + L.k_off + swz<RB>(j, part + cc * PARTS));
             const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
@@ -184,10 +262,14 @@ __global__ void __launch_bounds__(256)
               acc = fmaf(f, f, acc);
             }
           }
-          v = (bias[t] - gamma * acc) * kLog2e;
-          if (bias[t] == kNegInf) v = kNegInf;
         }
-        term[j] = v;
+        if (PARTS == 2) acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (part == 0 && j < NKP) {
+          float v = kNegInf;
+          if (j < nk && bias[t] != kNegInf)
+            v = (bias[t] - gamma * acc) * kLog2e;
+          term[j] = v;
+        }
       }
     }
     if (__syncthreads_or(!ok)) return;  // error recorded; all threads leave
@@ -228,8 +310,8 @@ __global__ void __launch_bounds__(256)
         sc[j][1] = fmaf(sc[j][1], g2, t2.y);
         sc[j][2] = fmaf(sc[j][2], g2, t2.x);
         sc[j][3] = fmaf(sc[j][3], g2, t2.y);
-        m0 = fmaxf(m0, fmaxf(sc[j][0], sc[j][1]));
-        m1 = fmaxf(m1, fmaxf(sc[j][2], sc[j][3]));
+        m0 = fmax3(m0, sc[j][0], sc[j][1]);
+        m1 = fmax3(m1, sc[j][2], sc[j][3]);
       }
       m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
       m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
@@ -237,17 +319,19 @@ __global__ void __launch_bounds__(256)
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
       const float s0 = m0 == kNegInf ? 0.f : m0;
       const float s1 = m1 == kNegInf ? 0.f : m1;
-      float l0 = 0.f, l1 = 0.f;
+      uint64_t l0x2 = 0, l1x2 = 0;
       uint32_t pa[NT][2];  // P as packed pairs: [tile][row g, row g + 8]
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
         const float p0 = fast_exp2(sc[j][0] - s0), p1 = fast_exp2(sc[j][1] - s0);
         const float p2 = fast_exp2(sc[j][2] - s1), p3 = fast_exp2(sc[j][3] - s1);
-        l0 += p0 + p1;
-        l1 += p2 + p3;
+        l0x2 = fadd2(l0x2, f2pk(p0, p1));
+        l1x2 = fadd2(l1x2, f2pk(p2, p3));
         pa[j][0] = pack_pair<T>(p0, p1);
         pa[j][1] = pack_pair<T>(p2, p3);
       }
+      const float2 l0p = f2upk(l0x2), l1p = f2upk(l1x2);
+      float l0 = l0p.x + l0p.y, l1 = l1p.x + l1p.y;
       l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
       l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -293,8 +377,10 @@ __global__ void __launch_bounds__(256)
       if (done == uint32_t(W - 1)) {
         count[s] = 0;
         if (i + kStages < my_items) {
+          ItemCursor at;
+          at.init(int(blockIdx.x) + (i + kStages) * gstep, L);
           fence_proxy_async_smem();
-          issue(i + kStages);
+          issue(i + kStages, at);
         }
       }
     }
@@ -305,7 +391,7 @@ int key_tile(int64_t nk) {
   return nk <= 32 ? 32 : nk <= 64 ? 64 : nk <= 80 ? 80 : 128;
 }
 
-template <typename T, int D, int NKP>
+template <typename T, int D, int NKP, int PARTS>
 cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
   const int64_t qmax = p.Nq < 128 ? p.Nq : 128;
   const int W = static_cast<int>((qmax + 15) / 16);
@@ -330,7 +416,7 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
       !make_tile_map(&tk, p.k, p.dtype, p.B, p.H, p.Nk, D, p.sk, NKP, D) ||
       !make_tile_map(&tv, p.v, p.dtype, p.B, p.H, p.Nk, D, p.sv, NKP, D))
     return cudaErrorInvalidValue;
-  auto kern = rbf_small_kernel<T, D, NKP>;
+  auto kern = rbf_small_kernel<T, D, NKP, PARTS>;
   static std::atomic<int> configured[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
@@ -352,17 +438,28 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
                     smem, stream, tq, tk, tv, p, L);
 }
 
+// The key-term split: two threads per key when the CTA has at least two
+// threads per key of the tile.
+template <typename T, int D, int NKP>
+cudaError_t launch_k(const RbfProblem& p, cudaStream_t stream) {
+  const int64_t qmax = p.Nq < 128 ? p.Nq : 128;
+  const int64_t threads = 32 * ((qmax + 15) / 16);
+  return VECTRA_SMALL_SPLIT_KEYS && threads >= 2 * NKP
+             ? launch_t<T, D, NKP, 2>(p, stream)
+             : launch_t<T, D, NKP, 1>(p, stream);
+}
+
 template <typename T, int D>
 cudaError_t launch_d(const RbfProblem& p, cudaStream_t stream) {
   switch (key_tile(p.Nk)) {
     case 32:
-      return launch_t<T, D, 32>(p, stream);
+      return launch_k<T, D, 32>(p, stream);
     case 64:
-      return launch_t<T, D, 64>(p, stream);
+      return launch_k<T, D, 64>(p, stream);
     case 80:
-      return launch_t<T, D, 80>(p, stream);
+      return launch_k<T, D, 80>(p, stream);
     default:
-      return launch_t<T, D, 128>(p, stream);
+      return launch_k<T, D, 128>(p, stream);
   }
 }
 
