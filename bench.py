@@ -30,6 +30,8 @@ Rank 0 prints one JSON line with:
   (rank 0, N == 1 only);
 * extra.long_sequence (config 2, N == 1): benchmark config 4 (B=16, H=16,
   L=4096, D=128) through the tensor-core kernel, TFLOP/s by CUDA events;
+* extra.reference_triton_kernel (N == 1): the reference's own Triton kernel
+  on the same inputs and GPU, timed the same way, for context;
 * clocks: nvidia-smi samples taken while the GPU ran the kernel.
 
 `--impl reference` times the reference's CPU implementation of the path
@@ -492,6 +494,65 @@ def long_sequence_extra(gpu, calls=20):
     return out
 
 
+def reference_triton_extra(gpu, sets, calls=240):
+    """The reference's own GPU kernel on the same input sets, for context:
+    its launcher `rbf_attention_forward` (kernels/vectra_kernels/
+    spatial_rbf_attention.py:177-281, the Triton kernel the operator's CUDA
+    registration called, custom_ops.py:75-85), JIT-compiled by this image's
+    Triton for the B200, imported from the reference's unmodified install
+    in baseline/_ref (its module registers no operator). Calls replayed
+    from a CUDA graph and timed with CUDA events, like this library's.
+    None when the install or Triton is missing."""
+    ref = os.path.join(ROOT, 'baseline', '_ref')
+    if not os.path.isfile(os.path.join(ref, 'INSTALL.json')):
+        return None
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    try:
+        from vectra_kernels import spatial_rbf_attention  # pylint: disable=import-outside-toplevel
+    except ImportError as exc:
+        return {'unavailable': f'cannot import the reference kernel: {exc}'}
+    torch = gpu.torch
+    n = len(sets)
+
+    def step(i):
+        w = sets[i % n]
+        return spatial_rbf_attention.rbf_attention_forward(
+            w.q, w.k, w.v, w.scale, w.key_bias)
+
+    for i in range(max(3, n)):
+        step(i)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(gpu.dev)
+    side.wait_stream(torch.cuda.current_stream(gpu.dev))
+    per_graph = n * -(-12 // n)
+    with torch.cuda.stream(side):
+        for i in range(n):
+            step(i)
+        side.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for c in range(per_graph):
+                step(c)
+    stream = torch.cuda.current_stream(gpu.dev)
+    stream.wait_stream(side)
+    graph.replay()
+    reps = max(1, calls // per_graph)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    ms = e0.elapsed_time(e1) / (reps * per_graph)
+    return {'kernel': 'reference Triton kernel (spatial_rbf_attention.'
+                      'rbf_attention_forward), JIT-compiled for sm_100',
+            'ms_per_call': ms, 'calls': reps * per_graph}
+
+
 def run_vectra(args):
     sys.path.insert(0, ROOT)
     gpu = Gpu()
@@ -641,6 +702,15 @@ def run_vectra(args):
                         'ms_per_step': alt_step, 'steps': steps_alt,
                         'queries_per_gpu': alt['per_gpu'],
                         'global_batch': alt['global_batch']}
+    if not args.no_extra and world == 1:
+        ref_kernel = reference_triton_extra(gpu, sets[:max(1, min(3, len(
+            sets)))])
+        if ref_kernel is not None:
+            if 'ms_per_call' in ref_kernel:
+                ref_kernel['this_library_ms_per_call'] = region_ms / args.steps
+                ref_kernel['speedup'] = (ref_kernel['ms_per_call'] /
+                                         (region_ms / args.steps))
+            extra['reference_triton_kernel'] = ref_kernel
     if not args.no_extra and world == 1 and args.config == 2:
         extra['long_sequence'] = long_sequence_extra(gpu)
 
