@@ -27,7 +27,9 @@
 //    their latency overlaps it.
 //  * Item coordinates (b, h, query block) advance by a fixed step per item
 //    (no integer division in the loop); the row sums use packed f32x2
-//    adds.
+//    adds; when the key tile's last 8 keys are all padding (Nk <= NKP - 8,
+//    e.g. 65 keys in an 80-key tile) that n-tile of S is not computed and
+//    its P is zero.
 //  * S = Q K^T and O = P V on mma.sync m16n8k16 (bf16/f16 in, f32
 //    accumulate): Q fragments by ldmatrix, K fragments by ldmatrix, V
 //    fragments by ldmatrix.trans. All of a plane's keys are in the tile, so
@@ -52,6 +54,11 @@ namespace {
 #define VECTRA_SMALL_STAGES 2
 #endif
 constexpr int kStages = VECTRA_SMALL_STAGES;
+// 1: an 8-key tile of S whose keys are all padding (Nk <= NKP - 8) is not
+// computed.
+#ifndef VECTRA_SMALL_TRIM_KEYS
+#define VECTRA_SMALL_TRIM_KEYS 1
+#endif
 // 1: two threads per key form the key terms when the CTA has 2 NKP threads.
 #ifndef VECTRA_SMALL_SPLIT_KEYS
 #define VECTRA_SMALL_SPLIT_KEYS 1
@@ -89,8 +96,8 @@ __device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t addr,
   return old;
 }
 
-// Packed float32 pairs (sm_100a f32x2 arithmetic): logits and the
-// softmax's subtract and sum take one instruction per two elements.
+// Packed float32 pairs (sm_100a f32x2 arithmetic) for the softmax's row
+// sums.
 __device__ __forceinline__ uint64_t f2pk(float x, float y) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
@@ -99,11 +106,6 @@ __device__ __forceinline__ uint64_t f2pk(float x, float y) {
 __device__ __forceinline__ float2 f2upk(uint64_t v) {
   float2 r;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
 __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
@@ -147,7 +149,7 @@ struct ItemCursor {
 // PARTS threads (adjacent lanes) share a key's norm: each takes CH / PARTS
 // of its 16-byte chunks and they add their partial sums with a shuffle, so
 // the key terms are spread over every thread of the CTA.
-template <typename T, int D, int NKP, int PARTS>
+template <typename T, int D, int NKP, int PARTS, int NTV>
 __global__ void __launch_bounds__(256)
     rbf_small_kernel(const __grid_constant__ CUtensorMap tq,
                      const __grid_constant__ CUtensorMap tk,
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(256)
   constexpr int RB = D * 2;        // bytes per row (bf16/f16)
   constexpr int CH = RB / 16;      // 16-byte chunks per row
   constexpr int NT = NKP / 8;      // 8-key n-tiles of S
+  static_assert(NTV >= NT - 1 && NTV <= NT, "valid n-tiles");
   constexpr int KS = D / 16;       // 16-dim k-steps of S
   constexpr int DT = D / 8;        // 8-dim n-tiles of O
   // Key-term slots per thread: with two threads per key the CTA has at
@@ -297,14 +300,15 @@ __global__ void __launch_bounds__(256)
                                   2 * ks + ((lane >> 3) & 1)),
                   kb);
           mma16816<T>(sc[2 * np], qa[ks], kb[0], kb[1]);
-          mma16816<T>(sc[2 * np + 1], qa[ks], kb[2], kb[3]);
+          if (2 * np + 1 < NTV)
+            mma16816<T>(sc[2 * np + 1], qa[ks], kb[2], kb[3]);
         }
       }
       // Logits, exact row softmax over the quad sharing a row.
       const float g2 = 2.f * gamma * kLog2e;
       float m0 = kNegInf, m1 = kNegInf;
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
+      for (int j = 0; j < NTV; ++j) {
         const float2 t2 = *reinterpret_cast<const float2*>(&term[8 * j + 2 * c]);
         sc[j][0] = fmaf(sc[j][0], g2, t2.x);
         sc[j][1] = fmaf(sc[j][1], g2, t2.y);
@@ -322,7 +326,7 @@ __global__ void __launch_bounds__(256)
       uint64_t l0x2 = 0, l1x2 = 0;
       uint32_t pa[NT][2];  // P as packed pairs: [tile][row g, row g + 8]
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
+      for (int j = 0; j < NTV; ++j) {
         const float p0 = fast_exp2(sc[j][0] - s0), p1 = fast_exp2(sc[j][1] - s0);
         const float p2 = fast_exp2(sc[j][2] - s1), p3 = fast_exp2(sc[j][3] - s1);
         l0x2 = fadd2(l0x2, f2pk(p0, p1));
@@ -330,13 +334,16 @@ __global__ void __launch_bounds__(256)
         pa[j][0] = pack_pair<T>(p0, p1);
         pa[j][1] = pack_pair<T>(p2, p3);
       }
+#pragma unroll
+      for (int j = NTV; j < NT; ++j) pa[j][0] = pa[j][1] = 0u;  // padding
       const float2 l0p = f2upk(l0x2), l1p = f2upk(l1x2);
       float l0 = l0p.x + l0p.y, l1 = l1p.x + l1p.y;
       l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
       l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-      // O = P V.
+      // O = P V. (Separate accumulators for even and odd 16-key steps, to
+      // shorten the dependency chains, measured slower.)
       float o[DT][4];
 #pragma unroll
       for (int j = 0; j < DT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -391,7 +398,7 @@ int key_tile(int64_t nk) {
   return nk <= 32 ? 32 : nk <= 64 ? 64 : nk <= 80 ? 80 : 128;
 }
 
-template <typename T, int D, int NKP, int PARTS>
+template <typename T, int D, int NKP, int PARTS, int NTV>
 cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
   const int64_t qmax = p.Nq < 128 ? p.Nq : 128;
   const int W = static_cast<int>((qmax + 15) / 16);
@@ -416,7 +423,7 @@ cudaError_t launch_t(const RbfProblem& p, cudaStream_t stream) {
       !make_tile_map(&tk, p.k, p.dtype, p.B, p.H, p.Nk, D, p.sk, NKP, D) ||
       !make_tile_map(&tv, p.v, p.dtype, p.B, p.H, p.Nk, D, p.sv, NKP, D))
     return cudaErrorInvalidValue;
-  auto kern = rbf_small_kernel<T, D, NKP, PARTS>;
+  auto kern = rbf_small_kernel<T, D, NKP, PARTS, NTV>;
   static std::atomic<int> configured[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
@@ -444,9 +451,13 @@ template <typename T, int D, int NKP>
 cudaError_t launch_k(const RbfProblem& p, cudaStream_t stream) {
   const int64_t qmax = p.Nq < 128 ? p.Nq : 128;
   const int64_t threads = 32 * ((qmax + 15) / 16);
-  return VECTRA_SMALL_SPLIT_KEYS && threads >= 2 * NKP
-             ? launch_t<T, D, NKP, 2>(p, stream)
-             : launch_t<T, D, NKP, 1>(p, stream);
+  // The last 8-key tile is all padding when Nk <= NKP - 8.
+  const bool trim = VECTRA_SMALL_TRIM_KEYS && p.Nk <= NKP - 8;
+  if (VECTRA_SMALL_SPLIT_KEYS && threads >= 2 * NKP)
+    return trim ? launch_t<T, D, NKP, 2, NKP / 8 - 1>(p, stream)
+                : launch_t<T, D, NKP, 2, NKP / 8>(p, stream);
+  return trim ? launch_t<T, D, NKP, 1, NKP / 8 - 1>(p, stream)
+              : launch_t<T, D, NKP, 1, NKP / 8>(p, stream);
 }
 
 template <typename T, int D>
