@@ -892,8 +892,9 @@ def run_model_reference(args):
 def run_model(args):
     """Config 5 served whole: the reference's PriceTransformer (4 layers,
     bf16 blocks), compiled by the reference's compile_entry with every RBF
-    site rewritten to this library's operator (the one-file swap), after the
-    reference's numerics gate.
+    site rewritten to this library's operator (the one-file swap) and this
+    library's value-views pass (vectra_b200.fusion), after the reference's
+    numerics gate.
 
     value: predictions/s with the batches resident in HBM, one step = one
     compiled forward of a served batch (1,024 targets, or the rank's shard
@@ -912,6 +913,7 @@ def run_model(args):
     from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
     world, rank, dev = gpu.world, gpu.rank, gpu.dev
 
+    from vectra_b200 import fusion  # pylint: disable=import-outside-toplevel
     ref = reference_swap.load_reference()
     per_gpu, global_batch = model_batch(args, world)
     cfg = ref.model.ModelConfig(**workloads.PRICE_MODEL)
@@ -919,11 +921,21 @@ def run_model(args):
                                          block_dtype='bfloat16')
     torch.manual_seed(0)
     eager = ref.compile_entry.prepare(ref.model.PriceTransformer(cfg), spec)
-    compiled, report, compile_s = ref.compile_entry.compile_model(eager, spec)
-    if report.sites != cfg.num_layers or report.graph_break_count:
-        raise SystemExit(f'compile pass rewrote {report.sites} of '
-                         f'{cfg.num_layers} sites with '
-                         f'{report.graph_break_count} graph breaks')
+    # Served with this library's value-views pass (vectra_b200.fusion:
+    # the operator reads V from the projection instead of the copy the
+    # reference pass cut at; bit-identical); the reference pass alone is
+    # timed too, as extra.reference_pass_only.
+    torch._dynamo.reset()  # pylint: disable=protected-access
+    plain, plain_report, _ = ref.compile_entry.compile_model(eager, spec)
+    torch._dynamo.reset()  # pylint: disable=protected-access
+    with fusion.installed() as value_pass:
+        compiled, report, compile_s = ref.compile_entry.compile_model(
+            eager, spec)
+    for r in (plain_report, report):
+        if r.sites != cfg.num_layers or r.graph_break_count:
+            raise SystemExit(f'compile pass rewrote {r.sites} of '
+                             f'{cfg.num_layers} sites with '
+                             f'{r.graph_break_count} graph breaks')
     # The reference's serving check before traffic (load_bundle): compiled
     # vs eager on a seeded batch at rtol 1e-3 / atol 1e-3.
     gate, _ = ref.compile_entry.max_abs_error(compiled, eager, cfg, spec,
@@ -975,6 +987,24 @@ def run_model(args):
     region_ms = r0.elapsed_time(r1)
     ms_per_step = gpu.max_over_ranks(region_ms) / args.steps
     value = global_batch / (ms_per_step * 1e-3)
+
+    # The reference pass alone (the operator reads the copy of V), the same
+    # way, for comparison.
+    for i in range(3):
+        with torch.no_grad():
+            plain(*sets[i % MODEL_SETS])
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    gpu.barrier()
+    p0.record(stream)
+    for i in range(args.steps):
+        with torch.no_grad():
+            plain(*sets[i % MODEL_SETS])
+    p1.record(stream)
+    torch.cuda.synchronize()
+    gpu.barrier()
+    plain_ms = gpu.max_over_ranks(p0.elapsed_time(p1)) / args.steps
+    del plain
 
     # End to end: requests of 8 served batches from pinned host memory,
     # result read back to the host.
@@ -1036,7 +1066,13 @@ def run_model(args):
             'scaling': args.scaling, 'vs_baseline': None, 'dtype': 'bf16',
             'data': 'synthetic (seeded inputs, random-init weights)',
             'config': model_config_line(args, world),
+            'extra': {'reference_pass_only': {
+                'ms_per_step': plain_ms,
+                'value': global_batch / (plain_ms * 1e-3),
+                'note': 'the reference compile pass alone: the operator '
+                        'reads the contiguous copy of V'}},
             'compile': {'sites': report.sites, 'matches': report.matches,
+                        'value_views_rewired': value_pass.rewired,
                         'graph_count': report.graph_count,
                         'graph_break_count': report.graph_break_count,
                         'seconds': compile_s,

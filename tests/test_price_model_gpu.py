@@ -168,3 +168,43 @@ def test_serving_matches_the_reference_serving_loop(reference, bf16_model):
         assert torch.equal(got, want)
         pinned = [t.pin_memory() for t in host]
         assert torch.equal(ours.predict(pinned), want)
+
+
+def test_value_views_pass_keeps_the_outputs(reference):
+    # vectra_b200.fusion hands the operator the projection's V view instead
+    # of the contiguous copy the reference pass cut at. The operator reads
+    # the same values either way (bit for bit, below); the compiled model,
+    # whose other kernels Inductor may generate differently without the
+    # copy, stays within the reference's export gate, with the same four
+    # kernel launches.
+    from vectra_b200 import fusion  # pylint: disable=import-outside-toplevel
+    cfg, spec, eager, compiled, _ = _build(reference, 4, 'bfloat16')
+    torch._dynamo.reset()  # pylint: disable=protected-access
+    with fusion.installed() as p:
+        fused, report, _ = reference.compile_entry.compile_model(eager, spec)
+    assert report.sites == 4 and p.rewired == 4
+    reference.compile_entry.max_abs_error(fused, eager, cfg, spec, batches=2)
+    for seed in (31, 32):
+        inputs = workloads.price_model_inputs(BATCH, seed=seed, device='cuda',
+                                              config=vars(cfg))
+        with torch.no_grad():
+            before = vectra_b200.launch_count()
+            got = fused(*inputs)
+            torch.cuda.synchronize()
+            assert vectra_b200.launch_count() - before == 4
+            torch.testing.assert_close(got, eager(*inputs).float(),
+                                       rtol=1e-3, atol=1e-3)
+
+
+def test_operator_reads_a_strided_value_view_bit_for_bit():
+    # The site's layout: q, k, v head-split views of one [B, N, 3 * 256]
+    # projection; v as that view and as its contiguous copy.
+    gen = torch.Generator(device='cuda').manual_seed(41)
+    qkv = torch.randn(BATCH, 65, 3, 8, 32, device='cuda', generator=gen)
+    q, k, v = qkv.bfloat16().permute(2, 0, 3, 1, 4)
+    scale = torch.rand(1, 8, 1, 1, device='cuda', generator=gen) * 0.2
+    bias = torch.zeros(BATCH, 1, 1, 65, device='cuda', dtype=torch.bfloat16)
+    bias[::5, ..., 50:] = float('-inf')
+    strided = torch.ops.vectra.rbf_attention(q, k, v, scale, bias)
+    copied = torch.ops.vectra.rbf_attention(q, k, v.contiguous(), scale, bias)
+    assert torch.equal(strided, copied)
