@@ -431,28 +431,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
+      // Descriptors of the tile bases, built once: a descriptor's start
+      // address field holds addr >> 4 (14 bits; shared-memory offsets stay
+      // below 256 KB), so the descriptor of base + off (off a multiple of
+      // 16) is the base's plus off >> 4, one add per MMA.
+      const uint64_t dq0 = sw128_desc(sbase + Cfg::OFF_Q, 16, 1024);
+      const uint64_t dk0 = sw128_desc(sbase + Cfg::OFF_KV, 16, 1024);
+      const uint64_t dv0 =
+          sw128_desc(sbase + Cfg::OFF_KV + Cfg::K_BYTES, Cfg::BLOCK, 1024);
       auto qk = [&](int x, int t) {
-        const uint32_t st = sbase + Cfg::OFF_KV + (t % kStages) * Cfg::STAGE;
-        const uint32_t qa = sbase + Cfg::OFF_Q + x * Cfg::Q_TILE;
+        const uint64_t dq = dq0 + uint64_t((x * Cfg::Q_TILE) >> 4);
+        const uint64_t dk = dk0 + uint64_t(((t % kStages) * Cfg::STAGE) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * Cfg::BLOCK + (kk & 3) * 32;
-          tc_mma(tmem + Cfg::s_col(x), sw128_desc(qa + off, 16, 1024),
-                 sw128_desc(st + off, 16, 1024), IDESC_QK, kk > 0);
+          const uint32_t off = ((kk >> 2) * Cfg::BLOCK + (kk & 3) * 32) >> 4;
+          tc_mma(tmem + Cfg::s_col(x), dq + off, dk + off, IDESC_QK, kk > 0);
         }
         tc_commit(bar_s_full(x));
       };
       auto pv = [&](int x, int t) {
-        const uint32_t vt = sbase + Cfg::OFF_KV + (t % kStages) * Cfg::STAGE +
-                            Cfg::K_BYTES;
+        const uint64_t dv = dv0 + uint64_t(((t % kStages) * Cfg::STAGE) >> 4);
         // P_X: bf16 pairs in TMEM over S_X, 8 columns per 16 keys. V is
         // MN-major: 16 keys = two 8-row groups of 128 B (SBO 1024),
         // 64-dim blocks BLOCK bytes apart (LBO).
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk)
           tc_mma_ts(tmem + Cfg::o_col(x), tmem + Cfg::s_col(x) + kk * 8,
-                    sw128_desc(vt + kk * 16 * 128, Cfg::BLOCK, 1024),
-                    IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+                    dv + uint64_t((kk * 16 * 128) >> 4), IDESC_PV,
+                    (t > 0 || kk > 0) ? 1u : 0u);
       };
       ok = mbar_wait(bar_q, 0, p.err);
       if (ok) ok = mbar_wait(bar_kv_full(0), 0, p.err);
