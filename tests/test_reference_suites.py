@@ -1,4 +1,4 @@
-"""The reference's own CPU test suites, run against this library's operator
+"""The reference's own test suites, run against this library's operator
 through the one-file swap.
 
 `oracle/install_reference.py` (run by `__graft_entry__.build()` wherever
@@ -91,3 +91,17 @@ def test_reference_compiler_suites_pass_with_the_swap():
     assert rc == 0, out[-4000:]
     summary = _summary(out)
     assert ' passed' in summary and 'failed' not in summary, summary
+
+
+@pytest.mark.gpu
+def test_reference_operator_gpu_test_passes_on_this_librarys_kernels():
+    # The reference's GPU-marked test (kernels/tests/test_custom_op.py:
+    # test_cuda_dispatches_to_the_triton_kernel) with the swap: the CUDA
+    # call reaches this library's kernels and must match the reference's
+    # float64 oracle at its own tolerance.
+    rc, out = run_reference_suites(
+        ['kernels/tests/test_custom_op.py::'
+         'test_cuda_dispatches_to_the_triton_kernel'], extra=['-rs'])
+    assert rc == 0, out[-4000:]
+    summary = _summary(out)
+    assert '1 passed' in summary and 'skipped' not in summary, summary
