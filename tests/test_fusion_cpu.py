@@ -8,7 +8,6 @@ must not change (on CPU the whole compiled model stays bit-identical), and
 chains that are not pure copies are left alone.
 """
 
-import os
 import shutil
 
 import pytest
@@ -96,9 +95,16 @@ def test_copy_of_a_computed_tensor_is_bypassed():
 @pytest.mark.skipif(not reference_swap.installed(),
                     reason='the reference is not installed in baseline/_ref')
 def test_reference_model_compiled_with_the_pass_is_bit_identical():
+    from torch._inductor import config as inductor_config  # pylint: disable=import-outside-toplevel
+    # Inductor's CPU backend compiles and links OpenMP C++; the system
+    # compiler is the one whose OpenMP spec files are complete.
     system_gxx = shutil.which('g++', path='/usr/bin')
-    if system_gxx and 'CXX' not in os.environ.get('VECTRA_KEEP_CXX', ''):
-        os.environ['CXX'] = system_gxx  # Inductor's CPU code needs OpenMP
+    cxx = {'cpp.cxx': (None, system_gxx)} if system_gxx else {}
+    with inductor_config.patch(cxx):
+        _compile_and_compare()
+
+
+def _compile_and_compare():
     ref = reference_swap.load_reference()
     cfg = ref.model.ModelConfig(embedding_dim=32, attribute_dim=8,
                                 d_model=64, num_heads=2, num_layers=2,
