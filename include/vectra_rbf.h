@@ -83,6 +83,7 @@ typedef struct {
 #define VECTRA_FLAG_FORCE_DECODE  0x2u /* the Nq == 1 streaming kernel */
 #define VECTRA_FLAG_FORCE_TC      0x4u /* the tcgen05/TMEM tensor-core kernel */
 #define VECTRA_FLAG_FORCE_SMALL   0x10u /* the one-tile-per-plane kernel */
+#define VECTRA_FLAG_FORCE_SMALL_TC 0x20u /* its tcgen05/TMEM form */
 
 /* Kernels (vectra_rbf_select_kernel's result). */
 enum {
@@ -91,7 +92,9 @@ enum {
   VECTRA_KERNEL_DECODE = 2,   /* rbf_decode: Nq == 1, bulk-copy streaming */
   VECTRA_KERNEL_TC = 3,       /* rbf_tc: tcgen05 + TMEM, long sequences */
   /* 4 is retired (an Nq == 1 mma.sync kernel, never chosen automatically) */
-  VECTRA_KERNEL_SMALL = 5       /* rbf_small: Nk <= 128, mma.sync tiles */
+  VECTRA_KERNEL_SMALL = 5,      /* rbf_small: Nk <= 128, mma.sync tiles */
+  VECTRA_KERNEL_SMALL_TC = 6    /* rbf_small_tc: Nq <= 96, Nk <= 128 - D,
+                                   tcgen05 + TMEM, one plane per slot */
 };
 
 /* Arguments of one forward call.
@@ -121,7 +124,7 @@ VECTRA_API int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* s
 VECTRA_API int vectra_rbf_select_kernel(const vectra_rbf_args* args);
 
 /* Name of a VECTRA_KERNEL_* value ("none", "generic", "decode", "tc",
- * "small"; "invalid" for any other value). */
+ * "small", "small_tc"; "invalid" for any other value). */
 VECTRA_API const char* vectra_rbf_kernel_name(int kernel);
 
 /* Message for a status code. */

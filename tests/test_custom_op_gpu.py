@@ -86,7 +86,7 @@ def _projection_views(dtype=torch.bfloat16, B=3, N=11, H=4, D=32):
     return q, k, v, scale
 
 
-@pytest.mark.parametrize('kernel', ['auto', 'generic', 'small'])
+@pytest.mark.parametrize('kernel', ['auto', 'generic', 'small', 'small_tc'])
 def test_output_follows_the_projection_layout(kernel):
     from vectra_b200 import custom_ops  # pylint: disable=import-outside-toplevel
     q, k, v, scale = _projection_views()

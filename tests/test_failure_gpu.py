@@ -56,6 +56,7 @@ CASES = {
     'decode_masked': ((6, 3, 1, 72, 64), 'bf16', True),
     'decode_masked_2chunks': ((5, 2, 1, 200, 64), 'bf16', True),
     'small': ((3, 2, 33, 65, 32), 'bf16', True),
+    'small_tc': ((3, 2, 33, 65, 32), 'bf16', True),
     'tc': ((1, 2, 300, 200, 64), 'bf16', True),
     'generic': ((2, 3, 21, 37, 48), 'f32', True),
 }
@@ -92,6 +93,7 @@ def test_output_guard_bands_are_untouched(kernel):
                'decode_masked': _lib.FLAG_FORCE_DECODE,
                'decode_masked_2chunks': _lib.FLAG_FORCE_DECODE,
                'small': _lib.FLAG_FORCE_SMALL,
+               'small_tc': _lib.FLAG_FORCE_SMALL_TC,
                'tc': _lib.FLAG_FORCE_TC,
                'generic': _lib.FLAG_FORCE_GENERIC}[kernel]
     assert _lib.LIB.vectra_rbf_select_kernel(ctypes.byref(a)) >= 0, kernel

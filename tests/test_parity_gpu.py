@@ -47,6 +47,8 @@ def _kernels_for(q_shape, d, dv, dtype, nk):
     if (q_shape[2] >= 2 and nk <= 128 and d == dv and d in (32, 64)
             and dtype != 'f32'):
         kernels.append('small')
+        if q_shape[2] <= 96 and nk <= 128 - d:
+            kernels.append('small_tc')
     return kernels
 
 

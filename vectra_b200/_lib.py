@@ -21,9 +21,11 @@ ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE, ERR_FORCED = -8, -9, -10, -11
 # kernel selection flags
 FLAG_FORCE_GENERIC, FLAG_FORCE_DECODE, FLAG_FORCE_TC = 0x1, 0x2, 0x4
 FLAG_FORCE_SMALL = 0x10
+FLAG_FORCE_SMALL_TC = 0x20
 # kernels
 KERNEL_NONE, KERNEL_GENERIC, KERNEL_DECODE, KERNEL_TC = 0, 1, 2, 3
 KERNEL_SMALL = 5
+KERNEL_SMALL_TC = 6
 
 # Every symbol include/vectra_rbf.h declares.
 EXPORTED = (

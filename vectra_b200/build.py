@@ -32,7 +32,7 @@ LIB = os.path.join(PKG, 'libvectra_rbf.so')
 TORCH_EXT = os.path.join(PKG, '_vectra_rbf_torch.so')
 
 CU_SOURCES = ['capi.cu', 'rbf_generic.cu', 'rbf_decode.cu', 'rbf_tc.cu',
-              'rbf_small.cu', 'tma_maps.cu', 'scan.cu']
+              'rbf_small.cu', 'rbf_small_tc.cu', 'tma_maps.cu', 'scan.cu']
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 

@@ -137,7 +137,8 @@ int select(const RbfProblem& p, uint32_t flags) {
   constexpr uint32_t kKnownFlags = VECTRA_FLAG_FORCE_GENERIC |
                                    VECTRA_FLAG_FORCE_DECODE |
                                    VECTRA_FLAG_FORCE_TC |
-                                   VECTRA_FLAG_FORCE_SMALL;
+                                   VECTRA_FLAG_FORCE_SMALL |
+                                   VECTRA_FLAG_FORCE_SMALL_TC;
   if (flags & ~kKnownFlags) return VECTRA_ERR_FORCED;
   if (p.B == 0 || p.H == 0 || p.Nq == 0 || p.Dv == 0)
     return VECTRA_KERNEL_NONE;
@@ -148,10 +149,13 @@ int select(const RbfProblem& p, uint32_t flags) {
     return tc_supports(p) ? VECTRA_KERNEL_TC : VECTRA_ERR_FORCED;
   if (flags & VECTRA_FLAG_FORCE_SMALL)
     return small_supports(p) ? VECTRA_KERNEL_SMALL : VECTRA_ERR_FORCED;
+  if (flags & VECTRA_FLAG_FORCE_SMALL_TC)
+    return small_tc_supports(p) ? VECTRA_KERNEL_SMALL_TC : VECTRA_ERR_FORCED;
   // Nq == 1: the SIMT decode kernel (an mma.sync variant measured slower
   // on every serving shape tried and is not built).
   if (decode_supports(p)) return VECTRA_KERNEL_DECODE;
   if (tc_supports(p)) return VECTRA_KERNEL_TC;
+  if (small_tc_supports(p)) return VECTRA_KERNEL_SMALL_TC;
   if (small_supports(p)) return VECTRA_KERNEL_SMALL;
   return VECTRA_KERNEL_GENERIC;
 }
@@ -224,6 +228,9 @@ int vectra_rbf_attention_forward(const vectra_rbf_args* args, void* stream) {
     case VECTRA_KERNEL_SMALL:
       err = launch_small(p, s);
       break;
+    case VECTRA_KERNEL_SMALL_TC:
+      err = launch_small_tc(p, s);
+      break;
     default:
       err = launch_generic(p, s);
       break;
@@ -245,6 +252,8 @@ const char* vectra_rbf_kernel_name(int kernel) {
       return "tc";
     case VECTRA_KERNEL_SMALL:
       return "small";
+    case VECTRA_KERNEL_SMALL_TC:
+      return "small_tc";
     default:
       return "invalid";
   }

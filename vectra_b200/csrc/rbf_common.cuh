@@ -344,6 +344,8 @@ cudaError_t launch_tc(const RbfProblem& p, cudaStream_t stream);
 bool tc_supports(const RbfProblem& p);
 cudaError_t launch_small(const RbfProblem& p, cudaStream_t stream);
 bool small_supports(const RbfProblem& p);
+cudaError_t launch_small_tc(const RbfProblem& p, cudaStream_t stream);
+bool small_tc_supports(const RbfProblem& p);
 
 // TMA tensor maps (tma_maps.cu). A [B, H, N, D] bf16/f16 view with element
 // strides s (s[3] == 1) as a 4-D map with a box of `box_cols` columns by

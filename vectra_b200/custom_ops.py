@@ -100,13 +100,14 @@ def rbf_attention(q, k, v, scale, key_bias=None) -> torch.Tensor:
 KERNELS = {'generic': _lib.FLAG_FORCE_GENERIC,
            'decode': _lib.FLAG_FORCE_DECODE,
            'tc': _lib.FLAG_FORCE_TC,
-           'small': _lib.FLAG_FORCE_SMALL}
+           'small': _lib.FLAG_FORCE_SMALL,
+           'small_tc': _lib.FLAG_FORCE_SMALL_TC}
 
 
 def rbf_attention_with_kernel(q, k, v, scale, key_bias=None,
                               kernel: str = 'auto') -> torch.Tensor:
     """The same operator with the kernel pinned ('generic', 'decode', 'tc',
-    'small').
+    'small', 'small_tc').
 
     Raises ValueError when the pinned kernel cannot run the problem.
     """
@@ -132,7 +133,7 @@ def _describe(t):
 
 def kernel_for(q, k, v, scale, key_bias=None, kernel: str = 'auto') -> str:
     """Name of the kernel the operator launches for these tensors
-    ('decode', 'tc', 'small', 'generic' or 'none'); raises
+    ('decode', 'tc', 'small_tc', 'small', 'generic' or 'none'); raises
     ValueError when the arguments are invalid. Launches nothing."""
     import ctypes  # pylint: disable=import-outside-toplevel
     a = _lib.Args()
