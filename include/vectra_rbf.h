@@ -94,7 +94,7 @@ enum {
   /* 4 is retired (an Nq == 1 mma.sync kernel, never chosen automatically) */
   VECTRA_KERNEL_SMALL = 5,      /* rbf_small: Nk <= 128, mma.sync tiles */
   VECTRA_KERNEL_SMALL_TC = 6    /* rbf_small_tc: Nq <= 96, Nk <= 128 - D,
-                                   tcgen05 + TMEM, one plane per slot */
+                                   tcgen05 + TMEM; only when forced */
 };
 
 /* Arguments of one forward call.

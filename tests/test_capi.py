@@ -108,25 +108,29 @@ def test_config1_fp32_selects_decode():
 
 def test_short_key_lists_select_the_small_kernels():
     # The compiled model's sites: [1024, 8, 65, 32] strided views, on the
-    # tcgen05 form (Nq <= 96, Nk <= 128 - D).
+    # mma.sync form; the tcgen05 form (Nq <= 96, Nk <= 128 - D) only when
+    # forced.
     st = (65 * 768, 32, 768, 1)
     a = _args(B=1024, nq=65, nk=65, d=32, dv=32, bias_shape=(1024, 1, 1, 65),
               q_strides=st)
     a.k = _tensor((1024, 8, 65, 32), strides=st)
     a.v = _tensor((1024, 8, 65, 32), strides=st)
-    assert _select(a) == _lib.KERNEL_SMALL_TC
-    a.flags = _lib.FLAG_FORCE_SMALL
     assert _select(a) == _lib.KERNEL_SMALL
-    assert _select(_args(nq=96, nk=96, d=32, dv=32)) == _lib.KERNEL_SMALL_TC
-    assert _select(_args(nq=64, nk=64, d=64, dv=64)) == _lib.KERNEL_SMALL_TC
+    a.flags = _lib.FLAG_FORCE_SMALL_TC
+    assert _select(a) == _lib.KERNEL_SMALL_TC
+    for nq, nk, d in ((96, 96, 32), (64, 64, 64)):
+        assert _select(_args(nq=nq, nk=nk, d=d, dv=d)) == _lib.KERNEL_SMALL
+        assert _select(_args(nq=nq, nk=nk, d=d, dv=d,
+                             flags=_lib.FLAG_FORCE_SMALL_TC)) == (
+                                 _lib.KERNEL_SMALL_TC)
     # More queries than three TMEM lane quarters, or keys past the slot's
-    # S columns: the mma.sync form.
-    assert _select(_args(nq=97, nk=65, d=32, dv=32)) == _lib.KERNEL_SMALL
-    assert _select(_args(nq=65, nk=97, d=32, dv=32)) == _lib.KERNEL_SMALL
-    assert _select(_args(nq=65, nk=65, d=64, dv=64)) == _lib.KERNEL_SMALL
+    # S columns: not the tcgen05 form.
+    for nq, nk, d in ((97, 65, 32), (65, 97, 32), (65, 65, 64)):
+        assert _select(_args(nq=nq, nk=nk, d=d, dv=d)) == _lib.KERNEL_SMALL
+        assert _select(_args(nq=nq, nk=nk, d=d, dv=d,
+                             flags=_lib.FLAG_FORCE_SMALL_TC)) == (
+                                 _lib.ERR_FORCED)
     assert _select(_args(nq=2, nk=128, d=64, dv=64)) == _lib.KERNEL_SMALL
-    assert _select(_args(nq=97, nk=65, d=32, dv=32,
-                         flags=_lib.FLAG_FORCE_SMALL_TC)) == _lib.ERR_FORCED
     # fp32, more than 128 keys, or D outside {32, 64}: not this kernel.
     assert _select(_args(nq=65, nk=65, d=32, dv=32, dtype=_lib.F32)) == (
         _lib.KERNEL_GENERIC)
@@ -135,7 +139,7 @@ def test_short_key_lists_select_the_small_kernels():
     # Row strides that are not 16-byte multiples rule out the TMA boxes.
     a = _args(nq=65, nk=65, d=32, dv=32, q_strides=(8 * 65 * 40, 65 * 40, 40,
                                                        1))
-    assert _select(a) == _lib.KERNEL_SMALL_TC
+    assert _select(a) == _lib.KERNEL_SMALL
     a = _args(nq=65, nk=65, d=32, dv=32, q_strides=(8 * 65 * 36, 65 * 36, 36,
                                                        1))
     assert _select(a) == _lib.KERNEL_GENERIC

@@ -126,7 +126,23 @@ __device__ __forceinline__ uint32_t load_bias_bits(const RbfProblem& p,
   }
 }
 
-// The float value of bits from load_bias_bits.
+// The bits of a scale element, loaded like load_bias_bits (convert with
+// bias_bits_to_f32 and the scale's dtype).
+__device__ __forceinline__ uint32_t load_scale_bits(const RbfProblem& p,
+                                                    int64_t b, int64_t h) {
+  const int64_t idx = b * p.ss[0] + h * p.ss[1];
+  switch (p.scale_dtype) {
+    case VECTRA_F32:
+      return __ldg(static_cast<const unsigned int*>(p.scale) + idx);
+    case VECTRA_F16:
+    case VECTRA_BF16:
+      return __ldg(static_cast<const unsigned short*>(p.scale) + idx);
+    default:
+      return __float_as_uint(static_cast<float>(
+          __ldg(static_cast<const double*>(p.scale) + idx)));
+  }
+}
+// The float value of bits from load_bias_bits (or load_scale_bits).
 __device__ __forceinline__ float bias_bits_to_f32(uint32_t w, int dtype) {
   switch (dtype) {
     case VECTRA_F16:

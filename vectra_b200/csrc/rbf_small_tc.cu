@@ -7,14 +7,14 @@
 // and of the reference kernel (spatial_rbf_attention.py:120-166).
 //
 // Work item: one (b, h) plane. Persistent CTAs, one per SM, 16 warps:
-//  * warp 3, one lane: TMA producer. For each plane, Q (Nq rows rounded up
+//  * warp 3, one elected lane: TMA producer. For each plane, Q (Nq rows rounded up
 //    to 16), K and V (NKP rows) as boxes of 4-D tensor maps over the
 //    caller's strides, into a ring of stages (swizzled over the 64- or
 //    128-byte row, the canonical UMMA K-major layout; rows past Nq / Nk
 //    arrive as zeros).
 //  * warp 7: allocates 512 TMEM columns = 4 plane slots of 128 columns
 //    (S in the first NKP, overlaid by P as bf16/f16 pairs; O in the last
-//    D); lane 0 issues the MMAs.
+//    D); one elected lane (elect.sync) issues the MMAs.
 //    S = Q K^T is one M=128 x N=NKP tcgen05.mma per 16 dims with both
 //    operands in shared memory (Q rows past the box are whatever follows
 //    it in shared memory: they only produce S rows nobody reads). O = P V
@@ -23,7 +23,8 @@
 //    in order, so QK(i+4) overwrites slot i % 4's S/P after PV(i) read P.
 //  * warps 11 and 15: key terms (b_j - g ||k_j||^2) log2(e) of alternate
 //    planes, one lane per key, from the staged K tile; -inf for padded or
-//    masked keys. The bias loads are issued before the stage wait.
+//    masked keys. A plane's scale and bias loads are issued while the
+//    warp works on its previous plane.
 //  * softmax group x = 0..3 (warps 4x + q, q < ceil(Nq / 32)): planes
 //    x, x + 4, ... through TMEM slot x. Thread = query row = TMEM lane
 //    32q + lane: the S row into registers, logits 2 g log2(e) S_j + t_j
@@ -34,6 +35,13 @@
 //    rule (kernels/vectra_kernels/reference.py:146-152).
 // Plane slot x's O is rewritten by PV(i + 4) only after the group has read
 // O(i): the group arrives on P(i + 4)'s barrier after its epilogue of i.
+// Measured (config 5, B200): 48.1 us per site against 45.7 for the mma.sync
+// kernel (rbf_small.cu), so it runs only when forced
+// (VECTRA_FLAG_FORCE_SMALL_TC). Traced with clock64 per role and plane, one
+// plane per M=128 tile leaves the tensor core ~8% busy and makes each plane
+// a serial chain (S -> softmax -> P -> P V -> epilogue) through one of four
+// TMEM slots: the four softmax groups fall into lockstep pairs and each
+// SMSP idles between chains; removing every exp2 saved only 13%.
 // Every mbarrier wait is bounded (error word + early exit); before the
 // teardown the producer waits for the loads it issued and the MMA lane for
 // the MMAs it issued, so no copy or MMA is in flight when TMEM is freed.
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if (elect_one()) {
       int issued = 0;
       for (int i = 0; i < my; ++i) {
         const int s = i % NS;
@@ -196,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (elect_one()) {
       // K-major Q and K: 8-row groups RB * 8 bytes apart (SBO); a 16-dim
       // k-step is 32 bytes along the swizzled row. MN-major V: 8-key groups
       // RB * 8 bytes apart, one swizzle atom across its D columns; 16 keys
@@ -253,21 +261,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kKeyWarp0 || warp == kKeyWarp0 + 4) {
     // ----------------------------------------------------------- key terms
-    for (int i = warp == kKeyWarp0 ? 0 : 1; i < my; i += kKeyWarps) {
-      const int s = i % NS;
+    // The scale and bias of a warp's next plane are loaded (as raw bits)
+    // while it works on the current one: traced on B200, their
+    // global-memory latency, exposed once per plane, set the pace of the
+    // whole kernel.
+    uint32_t gamma_next = 0, bias_next[NB];
+    auto prefetch = [&](int i) {
       int b, h;
       plane_bh(i, b, h);
-      const float gamma = load_scale(p, b, h);
-      float bias[NB];
+      gamma_next = load_scale_bits(p, b, h);
 #pragma unroll
       for (int t = 0; t < NB; ++t) {
         const int j = lane + 32 * t;
-        bias[t] = (p.bias != nullptr && j < nk) ? load_bias(p, b, h, j) : 0.f;
+        bias_next[t] =
+            (p.bias != nullptr && j < nk) ? load_bias_bits(p, b, h, j) : 0u;
       }
+    };
+    const int first = warp == kKeyWarp0 ? 0 : 1;
+    if (first < my) prefetch(first);
+    for (int i = first; i < my; i += kKeyWarps) {
+      const int s = i % NS;
+      const uint32_t gamma_bits = gamma_next;
+      uint32_t bias_bits[NB];
+#pragma unroll
+      for (int t = 0; t < NB; ++t) bias_bits[t] = bias_next[t];
+      if (i + kKeyWarps < my) prefetch(i + kKeyWarps);
       ok = mbar_wait(kv_full(s), uint32_t((i / NS) & 1), p.err);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint8_t* ktile = smem + s * L.stage_bytes + L.k_off;
+      const float gamma = bias_bits_to_f32(gamma_bits, p.scale_dtype);
 #pragma unroll
       for (int t = 0; t < NB; ++t) {
         const int j = lane + 32 * t;
@@ -296,7 +319,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ay = fmaf(hi, hi, ay);
               }
             }
-            if (bias[t] != kNegInf) v = (bias[t] - gamma * (ax + ay)) * kLog2e;
+            const float bias =
+                p.bias != nullptr ? bias_bits_to_f32(bias_bits[t], p.bias_dtype)
+                                  : 0.f;
+            if (bias != kNegInf) v = (bias - gamma * (ax + ay)) * kLog2e;
           }
           terms[s * NKP + j] = v;
         }
@@ -310,11 +336,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_tm = tmem + (uint32_t(q * 32) << 16) + uint32_t(x * kSlotCols);
     const uint32_t o_tm = s_tm + kOCol;
     const int row = q * 32 + lane;
+    uint32_t scale_next = 0;  // the next plane's scale, loaded a plane ahead
+    if (x < my) {
+      int b, h;
+      plane_bh(x, b, h);
+      scale_next = load_scale_bits(p, b, h);
+    }
     for (int i = x, n = 0; i < my; i += kGroups, ++n) {
       const int s = i % NS;
       int b, h;
       plane_bh(i, b, h);
-      const float g2 = 2.f * load_scale(p, b, h) * kLog2e;
+      const uint32_t scale_bits = scale_next;
+      if (i + kGroups < my) {
+        int b1, h1;
+        plane_bh(i + kGroups, b1, h1);
+        scale_next = load_scale_bits(p, b1, h1);
+      }
       ok = mbar_wait(s_full(x), uint32_t(n & 1), p.err) &&
            mbar_wait(nk_full(s), uint32_t((i / NS) & 1), p.err);
       ok = __all_sync(0xffffffffu, ok);
@@ -326,6 +363,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       regs_tie<NV>(sv);
       // Logits in place, row max over four independent accumulators.
       const float* tj = terms + s * NKP;
+      const float g2 =
+          2.f * bias_bits_to_f32(scale_bits, p.scale_dtype) * kLog2e;
       const uint64_t g2x2 = f2pk(g2, g2);
       float mxa = kNegInf, mxb = kNegInf, mxc = kNegInf, mxd = kNegInf;
 #pragma unroll

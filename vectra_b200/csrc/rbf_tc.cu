@@ -19,11 +19,11 @@
 //    into TMEM over the S columns already read (bf16 pairs), and O is
 //    rescaled in TMEM only when the row max grew by more than 8 (a factor
 //    of 256, the lazy-rescaling rule).
-//  * warp 8, one lane: TMA producer. Q (both tiles) once, then K and V tiles
+//  * warp 8, one elected lane: TMA producer. Q (both tiles) once, then K and V tiles
 //    of 128 keys into a 2-stage ring (128-byte swizzled, the canonical UMMA
 //    K-major / MN-major layouts) via 4-D tensor maps over [B, H, N, D] with
 //    the caller's strides; each CTA loads its own tiles.
-//  * warp 9: allocates all 512 TMEM columns (S_A, S_B, O_A, O_B); lane 0
+//  * warp 9: allocates all 512 TMEM columns (S_A, S_B, O_A, O_B); one lane
 //    issues the MMAs, ping-ponging the tiles so the tensor core works on
 //    one tile while the other's softmax runs:
 //      QK_A(0) QK_B(0) | PV_A(t) QK_A(t+1) PV_B(t) QK_B(t+1) | ...
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   setmaxnreg_dec<kOtherRegs>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------- producer
-    if (lane == 0) {
+    if (elect_one()) {
       mbar_arrive_expect_tx(bar_q, Cfg::Q_BYTES);
       for (int x = 0; x < kTilesQ; ++x)
         for (int kb = 0; kb < Cfg::KB; ++kb)
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (elect_one()) {
       // Descriptors of the tile bases, built once: a descriptor's start
       // address field holds addr >> 4 (14 bits; shared-memory offsets stay
       // below 256 KB), so the descriptor of base + off (off a multiple of

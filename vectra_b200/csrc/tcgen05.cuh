@@ -9,6 +9,21 @@
 
 namespace vectra {
 namespace tc {
+// True in one lane of the (converged) warp: elect.sync's leader. Code that
+// issues tcgen05.mma / tcgen05.commit / TMA copies from one thread runs
+// under this instead of a lane-index test: measured on B200, a loop of
+// tcgen05.mma issued under `lane == 0` costs about 200 cycles per MMA,
+// under elect.sync 58-171 (M=128, N=32..256). The leader is the same lane
+// every time (the lowest active one), so the thread that commits is the
+// thread that issued.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile(
       "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::
