@@ -84,6 +84,12 @@ def parse_args(argv=None):
     p.add_argument('--no-extra', action='store_true',
                    help='skip the extra measurements (weak scaling at N > 1, '
                         'config 4 at N == 1)')
+    p.add_argument('--kernel', default='auto',
+                   choices=('auto', 'decode', 'tc', 'small', 'small_tc',
+                            'generic'),
+                   help='operator runs: pin the kernel (default: the one the '
+                        'library selects), e.g. to time or profile the '
+                        'tcgen05 form of the small kernel on config 5')
     p.add_argument('--profile', action='store_true',
                    help='warm-up and K steps only (for ncu): no clock soak, '
                         'no e2e, no CPU baseline, no JSON line')
@@ -179,12 +185,15 @@ def peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 'fallback'
 
 
-def ncu_traffic(config, name=None, key='dram_bytes_per_launch_full'):
+def ncu_traffic(config, name=None, key='dram_bytes_per_launch_full',
+                kernel=None):
     """DRAM bytes per launch from the committed ncu summary, if any
-    (profiles/<kernel>_config<config>.txt, or profiles/<name>.txt)."""
+    (profiles/rbf_<kernel>_config<config>.txt for the kernel the library
+    selects, or the pinned `kernel`; or profiles/<name>.txt)."""
     if name is None:
-        kernel = {4: 'rbf_tc', 5: 'rbf_small'}.get(config, 'rbf_decode')
-        name = f'{kernel}_config{config}'
+        if kernel in (None, 'auto'):
+            kernel = {4: 'tc', 5: 'small'}.get(config, 'decode')
+        name = f'rbf_{kernel}_config{config}'
     path = os.path.join(ROOT, 'profiles', f'{name}.txt')
     try:
         with open(path, encoding='utf-8') as f:
@@ -583,7 +592,15 @@ def run_vectra(args):
     w0 = sets[0]
     alg_bytes = workloads.algorithmic_bytes(w0)
     flops = workloads.algorithmic_flops(w0)
-    op = torch.ops.vectra.rbf_attention
+    if args.kernel == 'auto':
+        op = torch.ops.vectra.rbf_attention
+    else:
+        # The same operator with the kernel pinned (--kernel).
+        vectra_b200.kernel_for(*w0.tensors(), kernel=args.kernel)
+
+        def op(*a):
+            return vectra_b200.rbf_attention_with_kernel(
+                *a, kernel=args.kernel)
 
     def step(i):
         w = sets[i % n_sets]
@@ -662,8 +679,7 @@ def run_vectra(args):
             ready.record(copy_stream)
         compute_stream.wait_event(ready)
         with torch.cuda.stream(compute_stream):
-            out = vectra_b200.rbf_attention(d['q'], d['k'], d['v'],
-                                            d['scale'], d['key_bias'])
+            out = op(d['q'], d['k'], d['v'], d['scale'], d['key_bias'])
             out_hosts[i % 2].copy_(out, non_blocking=True)
             done = torch.cuda.Event()
             done.record(compute_stream)
@@ -733,9 +749,10 @@ def run_vectra(args):
         achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
         roof = {'bound': 'hbm', 'achieved': achieved, 'peak': hbm,
                 'unit': 'GB/s', 'frac': achieved / hbm,
-                'traffic': (ncu_traffic(args.config) * w0.batch /
-                            workloads.SHAPES[args.config][0]
-                            if ncu_traffic(args.config) else None),
+                'traffic': (ncu_traffic(args.config, kernel=args.kernel) *
+                            w0.batch / workloads.SHAPES[args.config][0]
+                            if ncu_traffic(args.config, kernel=args.kernel)
+                            else None),
                 'peak_kind': f'HBM copy, {peak_kind}',
                 'algorithmic_bytes_per_launch': alg_bytes,
                 'vs_8tbs': achieved / 8000.0}
@@ -759,7 +776,8 @@ def run_vectra(args):
             'data': 'synthetic (seeded; benchmark config shapes and '
                     'distributions)',
             'config': line_config(args, world),
-            'launch': {'kernel': vectra_b200.kernel_for(*w0.tensors()),
+            'launch': {'kernel': vectra_b200.kernel_for(
+                           *w0.tensors(), kernel=args.kernel),
                        'graph_calls': per_graph,
                        'queries_this_rank': w0.batch},
             'e2e': {'value': e2e_value, 'unit': unit,
