@@ -334,13 +334,14 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi clock and throttle-reason samples every 100 ms."""
+    """nvidia-smi clock, throttle-reason and utilisation samples every
+    100 ms."""
 
     QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,'
              'clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
              'clocks_event_reasons.hw_thermal_slowdown,'
              'clocks_event_reasons.sw_thermal_slowdown,'
-             'clocks_event_reasons.sw_power_cap')
+             'clocks_event_reasons.sw_power_cap,utilization.gpu')
 
     def __init__(self, device_index):
         self.proc = None
@@ -357,7 +358,7 @@ class ClockSampler:
     def stop(self):
         if self.proc is None:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [],
-                    'samples': 0}
+                    'samples': 0, 'util_max_pct': None}
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
@@ -365,7 +366,7 @@ class ClockSampler:
             self.proc.kill()
             out, _ = self.proc.communicate()
         rows = [r.split(',') for r in out.strip().splitlines() if r.strip()]
-        sm, smax, reasons = [], None, set()
+        sm, smax, reasons, util = [], None, set(), []
         names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
                  'sw_power_cap']
         for r in rows:
@@ -375,12 +376,13 @@ class ClockSampler:
                 for name, flag in zip(names, r[5:9]):
                     if flag.strip().lower() == 'active':
                         reasons.add(name)
+                util.append(float(r[9]))
             except (ValueError, IndexError):
                 continue
         loaded = [x for x in sm if smax and x > 0.5 * smax] or sm
         return {'sm_mhz': statistics.median(loaded) if loaded else None,
                 'sm_max_mhz': smax, 'reasons': sorted(reasons),
-                'samples': len(sm)}
+                'samples': len(sm), 'util_max_pct': max(util) if util else None}
 
 
 class Gpu:
@@ -410,6 +412,20 @@ class Gpu:
     def max_over_ranks(self, x):
         from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
         return sharding.max_over_ranks(x, device=self.dev)
+
+    def sum_over_ranks(self, x):
+        if not self.distributed:
+            return float(x)
+        t = self.torch.tensor([float(x)], dtype=self.torch.float64,
+                              device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def busy_gpus(self, clocks):
+        """How many ranks' GPUs nvidia-smi saw busy (utilisation above 0)
+        while the rank's sampler ran (the soak and the timed region)."""
+        util = clocks.get('util_max_pct')
+        return int(round(self.sum_over_ranks(1.0 if util and util > 0 else 0.0)))
 
     def close(self):
         if self.distributed:
@@ -644,6 +660,7 @@ def run_vectra(args):
     clocks = sampler.stop()
     slowest_ms = gpu.max_over_ranks(region_ms)
     ms_per_step = slowest_ms / args.steps
+    gpus_active = gpu.busy_gpus(clocks)
 
     # End to end through the public API: every step copies its inputs in
     # from pinned host memory, runs the operator and copies its result out.
@@ -788,6 +805,10 @@ def run_vectra(args):
                     # what bounds it: the host->device copy of the inputs
                     'h2d_gbs_per_gpu': h2d / (e2e_ms * 1e-3) / 1e9},
             'gpu_launches': launches,
+            'gpu_busy': {'gpus_active': gpus_active, 'n_gpus': world,
+                         'basis': 'ranks whose GPU nvidia-smi showed above '
+                                  '0% utilisation during the soak and '
+                                  'timed region'},
             'kernel_ms_per_launch': kernel_ms,
             'roofline': roof,
             'cpu_baseline': cpu,
