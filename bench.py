@@ -90,6 +90,11 @@ def parse_args(argv=None):
                    help='operator runs: pin the kernel (default: the one the '
                         'library selects), e.g. to time or profile the '
                         'tcgen05 form of the small kernel on config 5')
+    p.add_argument('--shard-of', type=int, default=1, metavar='N',
+                   help='one GPU only: time the shard that one rank of an '
+                        'N-GPU strong-scaling run gets (the per-GPU work '
+                        'of that run), e.g. for the small-shard launch '
+                        'list')
     p.add_argument('--profile', action='store_true',
                    help='warm-up and K steps only (for ncu): no clock soak, '
                         'no e2e, no CPU baseline, no JSON line')
@@ -586,6 +591,8 @@ def run_vectra(args):
     from vectra_b200 import sharding  # pylint: disable=import-outside-toplevel
     from vectra_b200 import workloads  # pylint: disable=import-outside-toplevel
     world, rank, dev = gpu.world, gpu.rank, gpu.dev
+    # --shard-of N on one GPU: this GPU plays rank 0 of N (strong scaling).
+    shards = args.shard_of if world == 1 else world
 
     def make_set(i, scaling):
         """Input set i on this rank: its shard of the identically seeded
@@ -594,7 +601,7 @@ def run_vectra(args):
             return workloads.make(args.config, device=dev,
                                   seed=1000 * rank + i)
         full = workloads.make(args.config, device=dev, seed=i)
-        lo, hi = sharding.shard_range(full.batch, world, rank)
+        lo, hi = sharding.shard_range(full.batch, shards, rank)
         part = full.slice(lo, hi)
         return workloads.Workload(
             part.config, part.dtype,
@@ -602,10 +609,13 @@ def run_vectra(args):
               for t in (part.q, part.k, part.v, part.scale, part.key_bias,
                         part.lengths)))
 
-    p = plan(args.config, args.scaling, world)
+    p = plan(args.config, args.scaling, shards)
     n_sets = p['n_sets']
     sets = [make_set(i, args.scaling) for i in range(n_sets)]
     w0 = sets[0]
+    if shards != world:
+        # The job is the shard: its queries, not the configured batch.
+        p['global_batch'] = w0.batch
     alg_bytes = workloads.algorithmic_bytes(w0)
     flops = workloads.algorithmic_flops(w0)
     if args.kernel == 'auto':
@@ -792,7 +802,9 @@ def run_vectra(args):
             'dtype': w0.dtype,
             'data': 'synthetic (seeded; benchmark config shapes and '
                     'distributions)',
-            'config': line_config(args, world),
+            'config': dict(line_config(args, world), **(
+                {'shard_of': shards, 'queries_this_gpu': w0.batch}
+                if shards != world else {})),
             'launch': {'kernel': vectra_b200.kernel_for(
                            *w0.tensors(), kernel=args.kernel),
                        'graph_calls': per_graph,
