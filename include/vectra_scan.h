@@ -117,12 +117,14 @@ VECTRA_API int vectra_scan_pq_topk(const vectra_scan_pq_args* args,
  * holds until the process exits. args->workspace is ignored.
  * VECTRA_ERR_UNSUPPORTED when the scan needs more scratch than that
  * (vectra_scan_workspace_bytes above VECTRA_SCAN_NOALLOC_SCRATCH_BYTES).
- * The first call on a device, with that device current, looks up the
- * array's device address and creates one event. Both stay cached for the
- * life of the process, so after a cudaDeviceReset of a device this entry
- * point must not be called on that device again. Every call on a device shares the array, and two calls in
- * flight on the GPU at once would race on it, so each call's stream first
- * waits for the previous call's kernels, whatever stream they ran on. A
+ * The first call on a device, with that device current, does the set-up:
+ * it looks up the array's device address and creates one event, so that
+ * first call should come before any stream capture. Both stay cached for
+ * the life of the process, so after a cudaDeviceReset of a device this
+ * entry point must not be called on that device again. Every call on a
+ * device shares the array, and two calls in flight on the GPU at once
+ * would race on it, so each call's stream first waits for the previous
+ * call's kernels, whatever stream they ran on. A
  * call writes every part of the array that it reads; nothing carries over
  * from the last call.
  * No counterpart in the reference: an entry point of this library only. */
