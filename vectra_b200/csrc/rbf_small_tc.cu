@@ -7,9 +7,9 @@
 // and of the reference kernel (spatial_rbf_attention.py:120-166).
 //
 // Work item: one (b, h) plane. Persistent CTAs, one per SM, 16 warps:
-//  * warp 3, one elected lane: TMA producer. For each plane, Q (Nq rows rounded up
-//    to 16), K and V (NKP rows) as boxes of 4-D tensor maps over the
-//    caller's strides, into a ring of stages (swizzled over the 64- or
+//  * warp 3, one elected lane: TMA producer. For each plane, Q (Nq rows
+//    rounded up to 16), K and V (NKP rows) as boxes of 4-D tensor maps over
+//    the caller's strides, into a ring of stages (swizzled over the 64- or
 //    128-byte row, the canonical UMMA K-major layout; rows past Nq / Nk
 //    arrive as zeros).
 //  * warp 7: allocates 512 TMEM columns = 4 plane slots of 128 columns
@@ -333,7 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if ((warp & 3) < L.quads) {
     // ------------------------------------------- softmax group x, quadrant q
     const int x = warp >> 2, q = warp & 3;
-    const uint32_t s_tm = tmem + (uint32_t(q * 32) << 16) + uint32_t(x * kSlotCols);
+    const uint32_t s_tm =
+        tmem + (uint32_t(q * 32) << 16) + uint32_t(x * kSlotCols);
     const uint32_t o_tm = s_tm + kOCol;
     const int row = q * 32 + lane;
     uint32_t scale_next = 0;  // the next plane's scale, loaded a plane ahead

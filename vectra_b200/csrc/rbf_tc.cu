@@ -19,10 +19,10 @@
 //    into TMEM over the S columns already read (bf16 pairs), and O is
 //    rescaled in TMEM only when the row max grew by more than 8 (a factor
 //    of 256, the lazy-rescaling rule).
-//  * warp 8, one elected lane: TMA producer. Q (both tiles) once, then K and V tiles
-//    of 128 keys into a 2-stage ring (128-byte swizzled, the canonical UMMA
-//    K-major / MN-major layouts) via 4-D tensor maps over [B, H, N, D] with
-//    the caller's strides; each CTA loads its own tiles.
+//  * warp 8, one elected lane: TMA producer. Q (both tiles) once, then K and
+//    V tiles of 128 keys into a 2-stage ring (128-byte swizzled, the
+//    canonical UMMA K-major / MN-major layouts) via 4-D tensor maps over
+//    [B, H, N, D] with the caller's strides; each CTA loads its own tiles.
 //  * warp 9: allocates all 512 TMEM columns (S_A, S_B, O_A, O_B); one lane
 //    issues the MMAs, ping-ponging the tiles so the tensor core works on
 //    one tile while the other's softmax runs:
