@@ -109,6 +109,11 @@ def parse_args(argv=None):
         p.error('--model needs --config 5')
     if args.scan and args.model:
         p.error('--scan and --model are separate workloads')
+    if args.shard_of < 1:
+        p.error('--shard-of needs N >= 1')
+    if (args.shard_of > 1 or args.kernel != 'auto') and (args.scan or
+                                                         args.model):
+        p.error('--shard-of and --kernel apply to the operator runs only')
     return args
 
 

@@ -95,6 +95,29 @@ def test_traffic_figures_come_from_the_committed_profiles(config, kernel):
     assert traffic is not None and traffic > 1e8
 
 
+def test_pinned_kernel_traffic_comes_from_its_own_profile():
+    assert bench.parse_args([]).kernel == 'auto'
+    a = bench.parse_args(['--config', '5', '--kernel', 'small_tc'])
+    assert a.kernel == 'small_tc'
+    small = bench.ncu_traffic(5)
+    pinned = bench.ncu_traffic(5, kernel='small_tc')
+    assert small is not None and pinned is not None and pinned > 1e8
+    assert pinned != small  # profiles/rbf_small_tc_config5.txt
+    assert bench.ncu_traffic(5, kernel='auto') == small
+
+
+def test_shard_of_options():
+    assert bench.parse_args([]).shard_of == 1
+    assert bench.parse_args(['--shard-of', '8']).shard_of == 8
+    for bad in (['--shard-of', '0'], ['--shard-of', '4', '--scan', 'l2'],
+                ['--config', '5', '--model', '--kernel', 'small'],
+                ['--kernel', 'nonesuch']):
+        with pytest.raises(SystemExit):
+            bench.parse_args(bad)
+    # One GPU playing rank 0 of 8 times the shard an 8-GPU run gives a rank.
+    assert bench.plan(2, 'strong', 8)['per_gpu'] == 128
+
+
 def test_model_mode_needs_config_5():
     with pytest.raises(SystemExit):
         bench.parse_args(['--model'])
