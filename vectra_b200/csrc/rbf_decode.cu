@@ -630,9 +630,12 @@ struct DecodeLauncher {
 // Masked problems (a key bias is given): exact-size items in a byte ring.
 // ---------------------------------------------------------------------------
 // The items are those above, (plane slot g, chunk c), with chunks of up to
-// 128 keys, but an item occupies exactly the shared memory it needs: the q
-// row and the key and value rows lo..hi (its first and last keys with a
-// finite bias), packed from row 0. kMaskProducers producer warps, which make
+// 128 keys, but an item occupies exactly the shared memory it needs: the
+// key and value rows lo..hi (its first and last keys with a finite bias),
+// packed from row 0 (the consumer loads the plane's q row from global memory
+// itself, before it waits for the plane's first item: one bulk copy fewer
+// per item for the producer, whose copy issue paces this kernel; config 3
+// 135.5 -> 131.1 us). kMaskProducers producer warps, which make
 // no global loads (their release stores would wait for them), each work
 // through every kMaskProducers-th item in order, in their own quarter of a
 // byte ring: item i uses slot i % kMaskSlots (an mbarrier for its rows, one
@@ -807,7 +810,9 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
         }
       }
       const int nrows = hi >= lo ? hi - lo + 1 : 0;
-      const int sz = (QB + nrows * (D + DV) * ES + 127) & ~127;
+      // Key and value rows only (the consumer reads q from global memory);
+      // a fully masked item still takes 128 bytes.
+      const int sz = max(128, (nrows * (D + DV) * ES + 127) & ~127);
       // Allocate [off, off + sz) after the live region, freeing done items
       // in order (lane 0 reads the flags; the warp agrees on the result).
       // The bias slot fetched next (item k + kMaskAhead) must be free too.
@@ -851,7 +856,7 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
       const int kbase = chunk * KC;
       uint8_t* st = ring + rbase + off;
       const uint32_t bar = smem_addr(&bars[slot]);
-      uint8_t* kd = st + QB;
+      uint8_t* kd = st;
       uint8_t* vd = kd + size_t(nrows) * D * ES;
       __syncwarp();
       if (elect_leader()) {
@@ -859,9 +864,7 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
         // Consumers' reads of the freed bytes and bias rows (released with
         // their done flags, acquired above) come before these async writes.
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(bar, QB + nrows * (D + DV) * ES);
-        bulk_g2s(smem_addr(st), gq + b * p.sq[0] + h * p.sq[1], QB, bar,
-                 stream_policy);
+        mbar_arrive_expect_tx(bar, nrows * (D + DV) * ES);
         if (nrows > 0 && L.k_contig)
           bulk_g2s(smem_addr(kd),
                    gk + b * p.sk[0] + h * p.sk[1] +
@@ -908,6 +911,15 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
     const int plane = int(blockIdx.x) + g * int(gridDim.x);
     const int b = plane / L.H, h = plane - b * L.H;
     const float g2 = load_scale(p, b, h) * kLog2e;
+    // The plane's q row straight from global memory, loaded before the wait
+    // for its first item so that the load's latency overlaps the wait.
+    T qreg[(D + 31) / 32];
+    {
+      const T* gqp = gq + b * p.sq[0] + h * p.sq[1];
+#pragma unroll
+      for (int t = 0; t < (D + 31) / 32; ++t)
+        if (lane + 32 * t < D) qreg[t] = gqp[lane + 32 * t];
+    }
     float m = kNegInf, l = 0.f;
     uint64_t acc[P];
 #pragma unroll
@@ -928,14 +940,17 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
       const int nrows = hi >= lo ? hi - lo + 1 : 0;
       const uint8_t* st = ring + md.x;
       const uint8_t* brow = bstage + slot * L.bias_row;
-      const uint8_t* ks = st + QB;
+      const uint8_t* ks = st;
       const uint8_t* vs = ks + size_t(nrows) * D * ES + vchunk * 16;
 
       if (chunk == 0) {
-        const T* sq = reinterpret_cast<const T*>(st);
-        for (int d = lane; d < D; d += 32) {
-          const int ch = d / E, e = d - (d / E) * E;
-          q32[((e >> 2) * C + ch) * 4 + (e & 3)] = to_f32(sq[d]);
+#pragma unroll
+        for (int t = 0; t < (D + 31) / 32; ++t) {
+          const int d = lane + 32 * t;
+          if (d < D) {
+            const int ch = d / E, e = d - (d / E) * E;
+            q32[((e >> 2) * C + ch) * 4 + (e & 3)] = to_f32(qreg[t]);
+          }
         }
         __syncwarp();
       }
