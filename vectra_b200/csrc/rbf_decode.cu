@@ -632,19 +632,19 @@ struct DecodeLauncher {
 // The items are those above, (plane slot g, chunk c), with chunks of up to
 // 128 keys, but an item occupies exactly the shared memory it needs: the
 // key and value rows lo..hi (its first and last keys with a finite bias),
-// packed from row 0 (the consumer loads the plane's q row from global memory
-// itself, before it waits for the plane's first item: one bulk copy fewer
-// per item for the producer, whose copy issue paces this kernel; config 3
-// 135.5 -> 131.1 us). kMaskProducers producer warps, which make
-// no global loads (their release stores would wait for them), each work
-// through every kMaskProducers-th item in order, in their own quarter of a
-// byte ring: item i uses slot i % kMaskSlots (an mbarrier for its rows, one
-// for its bias row, a staging row for the bias and its ring placement); the
-// bias row of the producer's item kMaskAhead ahead is bulk-copied while item
-// i is issued; from the staged biases the producer finds lo..hi, allocates
-// the item, arms the slot and copies the rows. Consumer warps compute as
-// above and mark items done; each producer frees its ring quarter in item
-// order. With variable key counts (benchmark config 3: 8..128 valid keys per
+// packed from row 0. kMaskProducers producer warps each work through every
+// kMaskProducers-th item in order, in their own quarter of a byte ring:
+// item i uses slot i % kMaskSlots (an mbarrier for its rows and its ring
+// placement). From the item's biases (loaded two of the producer's items
+// ahead) the producer finds lo..hi, allocates the item, arms the slot, and
+// an elect.sync leader copies the rows and publishes the item. Consumer
+// warps load their plane's q row and each chunk's biases from global memory
+// themselves, before they wait for the item, compute as above and mark
+// items done; each producer frees its ring quarter in item order. A
+// per-item clock64 trace found the producers' copy issue pacing the kernel:
+// the q row and bias row no longer go through the ring (two bulk copies
+// fewer per item, and the bias staging rows' 16 KB back to the ring:
+// config 3 135.5 -> 128.5 us in a graph loop). With variable key counts (benchmark config 3: 8..128 valid keys per
 // query) the ring then holds as many bytes in flight as the live rows need,
 // instead of fixed stages sized for a full chunk (measured: 139 us against
 // 149 us for the fixed stages; one producer warp alone was the bottleneck at
@@ -658,10 +658,6 @@ constexpr int kMaskSlots = 64;
 #endif
 constexpr int kMaskProducers = VECTRA_MASK_PRODUCERS;  // producer warps
 static_assert(kMaskSlots % kMaskProducers == 0, "slots per producer");
-#ifndef VECTRA_MASK_AHEAD
-#define VECTRA_MASK_AHEAD 4
-#endif
-constexpr int kMaskAhead = VECTRA_MASK_AHEAD;  // bias rows fetched ahead
 #ifndef VECTRA_MASK_POLL_NS
 #define VECTRA_MASK_POLL_NS 128
 #endif
@@ -676,10 +672,7 @@ struct MaskLaunch {
   int nchunks;      // ceil(Nk / KC)
   int k_contig;
   int v_contig;
-  int bias_es;      // bytes per bias element (2 or 4)
-  int bias_row;     // bytes per staged bias row (KC * bias_es)
   int ring_bytes;   // multiple of 128
-  int stage_area;   // byte offset of the bias staging rows
   int warp_area;    // byte offset of the consumers' per-warp areas
 };
 
@@ -697,33 +690,22 @@ __device__ __forceinline__ bool wait_smem_equals_short(const int* ptr,
   return false;
 }
 
-// Bias element j of a staged row, exp2 domain.
-__device__ __forceinline__ float staged_bias(const uint8_t* row, int j,
-                                             int es, int dtype) {
-  const uint32_t w = es == 4 ? reinterpret_cast<const uint32_t*>(row)[j]
-                             : reinterpret_cast<const uint16_t*>(row)[j];
-  return bias_bits_to_f32(w, dtype) * kLog2e;
-}
-
 template <typename T, int D, int DV, int KC, int WARPS>
 __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
     rbf_decode_masked_kernel(RbfProblem p, MaskLaunch L) {
   using Cfg = DecodeCfg<T, D, DV, KC>;
   constexpr int ES = Cfg::ES, E = Cfg::E, P = Cfg::P, C = Cfg::C;
-  constexpr int CV = Cfg::CV, RV = Cfg::RV, QB = Cfg::QB, KPL = Cfg::KPL;
+  constexpr int CV = Cfg::CV, RV = Cfg::RV, KPL = Cfg::KPL;
   constexpr int NSLOT = kMaskSlots;
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Layout: ring | row mbarriers | bias mbarriers | item meta {offset, lo,
-  // hi, item} | done | bias staging rows | consumers' q32 and
-  // probabilities.
+  // Layout: ring | row mbarriers | item meta {offset, lo, hi, item} | done
+  // | consumers' q32 and probabilities.
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.ring_bytes);
-  uint64_t* bbars = bars + NSLOT;
-  int4* meta = reinterpret_cast<int4*>(bbars + NSLOT);
+  int4* meta = reinterpret_cast<int4*>(bars + NSLOT);
   int* done = reinterpret_cast<int*>(meta + NSLOT);
-  uint8_t* bstage = smem + L.stage_area;
 
   const T* __restrict__ gq = static_cast<const T*>(p.q);
   const T* __restrict__ gk = static_cast<const T*>(p.k);
@@ -740,7 +722,6 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(smem_addr(&bars[s]), 1);
-      mbar_init(smem_addr(&bbars[s]), 1);
       meta[s] = make_int4(0, 0, -1, -1);
       done[s] = -1;
     }
@@ -766,43 +747,38 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
     // elected lane, whose proxy fence and release store each take ~25
     // cycles (config 3: 138.8 -> 135.4 us in a 12-call graph loop; 138.4 us
     // in bench.py against 138.8-141.0 before).
-    // Bulk copy of item i's bias row into its slot's staging row.
-    auto fetch_bias = [&](int i) {
+    // Item i's key biases (lane j: keys j, j + 32, ...; raw bits), loaded
+    // two of the producer's items ahead with plain loads issued after the
+    // item's release store, so they have landed before the next release
+    // (a release store waits for its lane's outstanding loads).
+    auto load_bits = [&](int i, uint32_t (&bits)[KPL]) {
       const int g = i / nchunks, chunk = i - g * nchunks;
       const int plane = int(blockIdx.x) + g * int(gridDim.x);
       const int b = plane / L.H, h = plane - b * L.H;
       const int kbase = chunk * KC;
-      const uint32_t bytes = uint32_t(min(KC, nk - kbase) * L.bias_es);
-      const int s = i % NSLOT;
-      const uint8_t* src = static_cast<const uint8_t*>(p.bias) +
-                           (b * p.sb[0] + h * p.sb[1] + kbase) * L.bias_es;
-      mbar_arrive_expect_tx(smem_addr(&bbars[s]), bytes);
-      bulk_g2s(smem_addr(bstage + s * L.bias_row), src, bytes,
-               smem_addr(&bbars[s]), stream_policy);
+      const int cnt = min(KC, nk - kbase);
+#pragma unroll
+      for (int t = 0; t < KPL; ++t) {
+        const int j = lane + 32 * t;
+        bits[t] = j < cnt ? load_bias_bits(p, b, h, kbase + j) : 0u;
+      }
     };
-    for (int a = 0; a < kMaskAhead; ++a) {
-      const int i = pr + a * step;
-      if (i < n_items && elect_leader()) fetch_bias(i);
-    }
+    uint32_t bits_a[KPL], bits_b[KPL];
+    if (pr < n_items) load_bits(pr, bits_a);
+    if (pr + step < n_items) load_bits(pr + step, bits_b);
     int tail = pr;  // oldest item of this producer not yet freed
     int head = 0;   // next free byte of this producer's ring quarter
     bool ok = true;
     for (int k = pr; k < n_items && ok; k += step) {
       const int slot = k % NSLOT;
-      // The item's biases (exp2 domain, -inf past the last key) and its
-      // live key range.
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(smem_addr(&bbars[slot]),
-                                uint32_t((k / NSLOT) & 1), p.err));
-      if (!ok) break;
+      // The item's live key range from its biases (-inf past the last key).
       const int cnt = min(KC, nk - (k % nchunks) * KC);
-      const uint8_t* brow = bstage + slot * L.bias_row;
       int lo = KC, hi = -1;
 #pragma unroll
       for (int t = 0; t < KPL; ++t) {
         const int j = lane + 32 * t;
         const float bv =
-            j < cnt ? staged_bias(brow, j, L.bias_es, p.bias_dtype) : kNegInf;
+            j < cnt ? bias_bits_to_f32(bits_a[t], p.bias_dtype) : kNegInf;
         const unsigned live = __ballot_sync(0xffffffffu, bv != kNegInf);
         if (live) {
           lo = min(lo, 32 * t + __ffs(live) - 1);
@@ -815,9 +791,7 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
       const int sz = max(128, (nrows * (D + DV) * ES + 127) & ~127);
       // Allocate [off, off + sz) after the live region, freeing done items
       // in order (lane 0 reads the flags; the warp agrees on the result).
-      // The bias slot fetched next (item k + kMaskAhead) must be free too.
-      const int ahead = k + kMaskAhead * step;
-      const int need_free = ahead < n_items ? ahead : k;
+      const int need_free = k;
       int off = -1;
       for (uint32_t it = 0; it < kSleepWaitLimit; ++it) {
         int t_new = tail, ub = 0;
@@ -893,9 +867,12 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
       }
       __syncwarp();
       if (elect_leader()) {
-        if (ahead < n_items) fetch_bias(ahead);
         st_release_smem(&meta[slot].w, k);
       }
+      // The next item's biases are already here; fetch the one after.
+#pragma unroll
+      for (int t = 0; t < KPL; ++t) bits_a[t] = bits_b[t];
+      if (k + 2 * step < n_items) load_bits(k + 2 * step, bits_b);
     }
     return;
   }
@@ -928,6 +905,16 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
     for (int chunk = 0; chunk < nchunks; ++chunk) {
       const int i = g * nchunks + chunk;
       const int slot = i % NSLOT;
+      // This chunk's key biases, loaded before the wait for its rows.
+      uint32_t cbits[KPL];
+      {
+        const int kbase = chunk * KC, cnt = min(KC, nk - kbase);
+#pragma unroll
+        for (int t = 0; t < KPL; ++t) {
+          const int j = lane + 32 * t;
+          cbits[t] = j < cnt ? load_bias_bits(p, b, h, kbase + j) : 0u;
+        }
+      }
       if (!wait_smem_equals_short(&meta[slot].w, i, p.err) ||
           !(VECTRA_MASK_CONSUMER_SLEEP
                 ? mbar_wait_sleep(smem_addr(&bars[slot]),
@@ -939,7 +926,6 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
       const int lo = md.y, hi = md.z;
       const int nrows = hi >= lo ? hi - lo + 1 : 0;
       const uint8_t* st = ring + md.x;
-      const uint8_t* brow = bstage + slot * L.bias_row;
       const uint8_t* ks = st;
       const uint8_t* vs = ks + size_t(nrows) * D * ES + vchunk * 16;
 
@@ -1002,7 +988,7 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
             ((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y));
         sc[t] = (j >= lo && j <= hi)
                     ? fmaf(-g2, dist,
-                           staged_bias(brow, j, L.bias_es, p.bias_dtype))
+                           bias_bits_to_f32(cbits[t], p.bias_dtype) * kLog2e)
                     : kNegInf;
         cmax = fmaxf(cmax, sc[t]);
       }
@@ -1105,8 +1091,9 @@ __global__ void __launch_bounds__(32 * (WARPS + kMaskProducers), 1)
   }
 }
 
-// Whether the byte-ring kernel takes a biased problem: its bias rows must
-// be whole 16-byte-aligned runs that bulk copies can move.
+// Whether the byte-ring kernel takes a biased problem: an f32 / f16 / bf16
+// bias with unit key stride whose rows are whole 16-byte-aligned runs (the
+// problems it is built and tested for; others take the fixed stages).
 bool mask_ring_supports(const RbfProblem& p) {
   if (p.bias == nullptr) return false;
   int es = 0;
@@ -1131,12 +1118,9 @@ struct MaskLauncher {
 
   static cudaError_t launch(const RbfProblem& p, cudaStream_t stream) {
     const size_t budget = 227 * 1024;
-    const int bias_es = p.bias_dtype == VECTRA_F32 ? 4 : 2;
-    const size_t meta = size_t(kMaskSlots) * (8 + 8 + 16 + 4);
-    const size_t stage = size_t(kMaskSlots) * KC * bias_es;
+    const size_t meta = size_t(kMaskSlots) * (8 + 16 + 4);
     const size_t warps_b = size_t(WARPS) * Cfg::WARP_BYTES;
-    const size_t ring =
-        (budget - meta - stage - warps_b - 256) & ~size_t(127);
+    const size_t ring = (budget - meta - warps_b - 256) & ~size_t(127);
     // Each producer's quarter of the ring must hold a full item.
     if (ring / kMaskProducers <
         size_t(Cfg::QB + KC * (D + DV) * Cfg::ES + 256))
@@ -1147,11 +1131,8 @@ struct MaskLauncher {
     L.nchunks = static_cast<int>((p.Nk + KC - 1) / KC);
     L.k_contig = p.sk[2] == D;
     L.v_contig = p.sv[2] == DV;
-    L.bias_es = bias_es;
-    L.bias_row = KC * bias_es;
     L.ring_bytes = static_cast<int>(ring);
-    L.stage_area = static_cast<int>((ring + meta + 127) & ~size_t(127));
-    L.warp_area = L.stage_area + static_cast<int>(stage);
+    L.warp_area = static_cast<int>((ring + meta + 127) & ~size_t(127));
     const size_t smem = size_t(L.warp_area) + warps_b;
     int64_t blocks = L.n_planes;
     const int64_t cap = device_sm_count();
